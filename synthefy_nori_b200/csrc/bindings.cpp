@@ -1,0 +1,42 @@
+// Python bindings of the native operator library (module synthefy_nori_b200._C).
+#include <torch/extension.h>
+
+namespace nori {
+torch::Tensor gemm_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::optional<torch::Tensor>& row_scale,
+                        const c10::optional<torch::Tensor>& bias, const torch::Tensor& status, int64_t bn);
+torch::Tensor gemm_swiglu(const torch::Tensor& A, const torch::Tensor& B, const c10::optional<torch::Tensor>& row_scale,
+                          const torch::Tensor& status, int64_t bn);
+torch::Tensor gemm_residual(const torch::Tensor& A, const torch::Tensor& B, const torch::Tensor& resid, double alpha,
+                            const c10::optional<torch::Tensor>& sumsq, const torch::Tensor& status, int64_t bn);
+void gemm_f32_out(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& out, bool accumulate,
+                  const torch::Tensor& status, int64_t bn);
+void gemm_headmajor(const torch::Tensor& A, const torch::Tensor& B, const c10::optional<torch::Tensor>& row_scale,
+                    torch::Tensor& out, int64_t T, int64_t n_rows, int64_t J, int64_t H, int64_t D, int64_t Dp,
+                    const torch::Tensor& status, int64_t bn);
+torch::Tensor rms_scale(const torch::Tensor& x, double eps);
+torch::Tensor sumsq_to_scale(const torch::Tensor& ssq, int64_t E, double eps);
+std::vector<torch::Tensor> pinball_fused(const torch::Tensor& pred, const torch::Tensor& target,
+                                         const torch::Tensor& quantiles, const torch::Tensor& inv_var, int64_t nq,
+                                         double tail_w, double mono_w, double mse_w);
+void grad_sumsq(const torch::Tensor& g, torch::Tensor& out);
+void adamw_ema(torch::Tensor& p, const torch::Tensor& g, torch::Tensor& m, torch::Tensor& v,
+               const c10::optional<torch::Tensor>& ema, const c10::optional<torch::Tensor>& pbf,
+               const c10::optional<torch::Tensor>& norm_sq, double lr, double beta1, double beta2, double eps,
+               double wd, int64_t step, double ema_decay, double max_norm, double grad_scale);
+std::vector<torch::Tensor> quantize_int8(const torch::Tensor& x);
+}  // namespace nori
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "Nori B200 native kernels (sm_100a)";
+  m.def("gemm_bf16", &nori::gemm_bf16);
+  m.def("gemm_swiglu", &nori::gemm_swiglu);
+  m.def("gemm_residual", &nori::gemm_residual);
+  m.def("gemm_f32_out", &nori::gemm_f32_out);
+  m.def("gemm_headmajor", &nori::gemm_headmajor);
+  m.def("rms_scale", &nori::rms_scale);
+  m.def("sumsq_to_scale", &nori::sumsq_to_scale);
+  m.def("pinball_fused", &nori::pinball_fused);
+  m.def("grad_sumsq", &nori::grad_sumsq);
+  m.def("adamw_ema", &nori::adamw_ema);
+  m.def("quantize_int8", &nori::quantize_int8);
+}

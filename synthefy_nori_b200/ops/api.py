@@ -1,1 +1,112 @@
-def _placeholder(): pass
+"""Python entry points of the native kernels.
+
+Every function requires CUDA tensors and the built extension; there is no silent
+fallback (``lib()`` raises if ``_C`` is missing).  The fp32 PyTorch references used
+by the numerics tests live in ``synthefy_nori_b200.ops.reference``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+__all__ = [
+    "gemm",
+    "gemm_swiglu",
+    "gemm_residual",
+    "gemm_f32",
+    "gemm_headmajor",
+    "rms_scale",
+    "sumsq_to_scale",
+    "pinball_loss_grad",
+    "grad_sumsq",
+    "adamw_ema_step",
+    "quantize_int8",
+    "status_word",
+    "interleave_swiglu_weights",
+]
+
+_STATUS: dict[int, torch.Tensor] = {}
+
+
+def _lib():
+    from synthefy_nori_b200.ops import lib
+
+    return lib()
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 word that kernels set on a bounded-wait timeout (0 = ok)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _STATUS.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _STATUS[idx] = t
+    return t
+
+
+def check_status(device: torch.device) -> None:
+    code = int(status_word(device).item())
+    if code != 0:
+        raise RuntimeError(f"native kernel reported a bounded-wait timeout (status code {code})")
+
+
+def gemm(a: torch.Tensor, w: torch.Tensor, row_scale=None, bias=None, bn: int = 0) -> torch.Tensor:
+    """bf16 ``(a @ w.T) * row_scale[:, None] + bias`` on tcgen05 (fp32 accumulation)."""
+    return _lib().gemm_bf16(a, w, row_scale, bias, status_word(a.device), bn)
+
+
+def gemm_swiglu(a: torch.Tensor, w_interleaved: torch.Tensor, row_scale=None, bn: int = 0) -> torch.Tensor:
+    """``silu(a W_g^T r) * (a W_u^T r)`` with gate/up rows interleaved in one weight."""
+    return _lib().gemm_swiglu(a, w_interleaved, row_scale, status_word(a.device), bn)
+
+
+def gemm_residual(a, w, resid, alpha: float, sumsq=None, bn: int = 0) -> torch.Tensor:
+    """bf16 ``resid + alpha * (a @ w.T)``; adds each new row's sum of squares to ``sumsq``."""
+    return _lib().gemm_residual(a, w, resid, float(alpha), sumsq, status_word(a.device), bn)
+
+
+def gemm_f32(a, w, out=None, accumulate: bool = False, bn: int = 0) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(a.shape[0], w.shape[0], device=a.device, dtype=torch.float32)
+    _lib().gemm_f32_out(a, w, out, accumulate, status_word(a.device), bn)
+    return out
+
+
+def gemm_headmajor(a, w, out, *, T, n_rows, J, H, D, Dp, row_scale=None, bn: int = 0):
+    _lib().gemm_headmajor(a, w, row_scale, out, T, n_rows, J, H, D, Dp, status_word(a.device), bn)
+    return out
+
+
+def rms_scale(x: torch.Tensor, eps: float) -> torch.Tensor:
+    return _lib().rms_scale(x, float(eps))
+
+
+def sumsq_to_scale(ssq: torch.Tensor, E: int, eps: float) -> torch.Tensor:
+    return _lib().sumsq_to_scale(ssq, int(E), float(eps))
+
+
+def pinball_loss_grad(pred, target, quantiles, inv_var, nq: int, tail_w=0.0, mono_w=0.0, mse_w=0.0):
+    """Fused pinball objective: returns (loss [1] fp32, d loss / d pred)."""
+    loss, grad = _lib().pinball_fused(pred, target, quantiles, inv_var, int(nq), float(tail_w), float(mono_w), float(mse_w))
+    return loss, grad
+
+
+def grad_sumsq(g: torch.Tensor, out: torch.Tensor) -> None:
+    _lib().grad_sumsq(g, out)
+
+
+def adamw_ema_step(p, g, m, v, *, lr, beta1, beta2, eps, wd, step, ema=None, p_bf16=None, norm_sq=None,
+                   ema_decay=0.999, max_norm=0.0, grad_scale=1.0) -> None:
+    _lib().adamw_ema(p, g, m, v, ema, p_bf16, norm_sq, float(lr), float(beta1), float(beta2), float(eps), float(wd),
+                     int(step), float(ema_decay), float(max_norm), float(grad_scale))
+
+
+def quantize_int8(x: torch.Tensor):
+    """Per-row (last dim) absmax int8: returns (q int8, scale fp32 with last dim 1)."""
+    q, s = _lib().quantize_int8(x.contiguous())
+    return q, s
+
+
+def interleave_swiglu_weights(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """[h, E] gate and up weights -> [2h, E] with rows (gate_0, up_0, gate_1, up_1, ...)."""
+    return torch.stack((w_gate, w_up), 1).reshape(-1, w_gate.shape[1])

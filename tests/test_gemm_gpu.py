@@ -1,0 +1,85 @@
+"""tcgen05 GEMM family vs an fp32 PyTorch reference of the same op."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from synthefy_nori_b200 import ops  # noqa: E402
+
+
+def _ref(a, w):
+    return a.float() @ w.float().T
+
+
+def _rand(*shape, scale=1.0):
+    return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (300, 448, 448), (1000, 1344, 448), (257, 96, 128), (4096, 896, 896), (77, 352, 352)])
+@pytest.mark.parametrize("bn", [0, 128, 256])
+def test_gemm_plain(M, N, K, bn):
+    torch.manual_seed(0)
+    a, w = _rand(M, K), _rand(N, K, scale=K ** -0.5)
+    rs = torch.rand(M, device="cuda") + 0.5
+    bias = torch.randn(N, device="cuda")
+    out = ops.gemm(a, w, rs, bias, bn=bn)
+    ref = _ref(a, w) * rs[:, None] + bias
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
+    ops.check_status(a.device)
+
+
+def test_gemm_strided_a():
+    torch.manual_seed(1)
+    big = _rand(513, 3 * 448)
+    a = big[:, 448:896]  # row stride 1344
+    w = _rand(448, 448, scale=448 ** -0.5)
+    out = ops.gemm(a, w)
+    torch.testing.assert_close(out.float(), _ref(a, w), atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("M,E,H", [(500, 448, 896), (129, 128, 256)])
+def test_gemm_swiglu(M, E, H):
+    torch.manual_seed(2)
+    a = _rand(M, E)
+    wg, wu = _rand(H, E, scale=E ** -0.5), _rand(H, E, scale=E ** -0.5)
+    rs = torch.rand(M, device="cuda") + 0.5
+    out = ops.gemm_swiglu(a, ops.interleave_swiglu_weights(wg, wu), rs)
+    g = _ref(a, wg) * rs[:, None]
+    u = _ref(a, wu) * rs[:, None]
+    ref = torch.nn.functional.silu(g) * u
+    torch.testing.assert_close(out.float(), ref, atol=3e-2, rtol=3e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(700, 448, 896), (64, 128, 128)])
+def test_gemm_residual(M, N, K):
+    torch.manual_seed(3)
+    a, w, r = _rand(M, K), _rand(N, K, scale=K ** -0.5), _rand(M, N)
+    ssq = torch.zeros(M, device="cuda")
+    out = ops.gemm_residual(a, w, r, 0.25, ssq)
+    ref = r.float() + 0.25 * _ref(a, w)
+    torch.testing.assert_close(out.float(), ref, atol=3e-2, rtol=3e-2)
+    torch.testing.assert_close(ssq, (out.float() ** 2).sum(1), atol=1e-2, rtol=1e-3)
+
+
+def test_gemm_f32_accumulate():
+    torch.manual_seed(4)
+    a, w = _rand(300, 256), _rand(200, 256)
+    out = torch.randn(300, 200, device="cuda")
+    ref = out + _ref(a, w)
+    ops.gemm_f32(a, w, out, accumulate=True)
+    torch.testing.assert_close(out, ref, atol=2e-2, rtol=1e-3)
+
+
+def test_gemm_headmajor():
+    torch.manual_seed(5)
+    B, n, T, H, D, Dp = 2, 37, 5, 2, 56, 64
+    E = 112
+    a = _rand(B * n * T, E)
+    w = _rand(3 * H * D, E, scale=E ** -0.5)
+    out = torch.zeros(B * T * 3 * H * n * Dp, device="cuda", dtype=torch.bfloat16)
+    ops.gemm_headmajor(a, w, out, T=T, n_rows=n, J=3, H=H, D=D, Dp=Dp)
+    ref = _ref(a, w).view(B, n, T, 3, H, D).permute(0, 2, 3, 4, 1, 5)  # B T J H n D
+    got = out.view(B, T, 3, H, n, Dp)
+    torch.testing.assert_close(got[..., :D].float(), ref, atol=2e-2, rtol=2e-2)
+    assert got[..., D:].abs().max().item() == 0
