@@ -1,0 +1,585 @@
+// Flash attention forward / backward for the two attention families of the Nori
+// encoder, reading and writing the framework's own layouts directly (no transposes):
+//
+//   * sequence (ICL) attention per (table, column, head) over context rows
+//     (reference model/layer.py:1407-1441: context self-attention and query->context
+//     cross-attention), Q/K/V head-major [.., H, rows, 64] written by the projection
+//     GEMM's head-major epilogue;
+//   * feature (within-row) attention per (table row, head) over the G+1 tokens of a
+//     row (reference model/layer.py:1391-1405).
+//
+// Head dim is padded to 64 in the inputs (padding columns are zero). Outputs go to a
+// generic 3-level strided layout, typically token-major [tokens, H * D] so the output
+// projection GEMM reads them as its A operand.
+//
+// Tiles: 64 query rows per CTA (4 warps x 16 rows), 64-key K/V tiles double-buffered
+// in shared memory with an XOR swizzle; QK^T and PV on mma.m16n8k16 bf16 with fp32
+// accumulation, online softmax in registers (exp2 with folded log2 e), natural-log LSE
+// saved for the backward pass and for partial-softmax merges.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "sm100.cuh"
+
+namespace nori {
+
+// bh -> (i0, i1, i2) with i2 fastest: i2 = bh % d2, i1 = (bh / d2) % d1, i0 = bh / (d1 d2)
+struct Layout3 {
+  int64_t s0, s1, s2, row;
+  int d1, d2;
+  __host__ __device__ int64_t offset(int64_t bh, int64_t r) const {
+    const int64_t i2 = bh % d2;
+    const int64_t t = bh / d2;
+    const int64_t i1 = t % d1;
+    const int64_t i0 = t / d1;
+    return i0 * s0 + i1 * s1 + i2 * s2 + r * row;
+  }
+};
+
+constexpr int kD = 64;      // padded head dim
+constexpr int kBlkQ = 64;   // query rows per CTA
+constexpr int kBlkK = 64;   // keys per tile
+constexpr int kAttnThreads = 128;
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Swizzled byte offset of (row, 16-byte chunk) in a [rows][64 bf16] tile.
+__device__ __forceinline__ int swz(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
+
+// Load a [64 rows][64 cols] bf16 tile; rows >= n_valid and columns >= d_valid read as 0.
+__device__ __forceinline__ void load_tile(uint8_t* tile, const __nv_bfloat16* base, int64_t row_stride, int row0,
+                                          int n_valid, int d_valid, int tid, int nthreads) {
+  for (int i = tid; i < 64 * 8; i += nthreads) {
+    const int r = i >> 3, c = i & 7;
+    const int gr = row0 + r;
+    int bytes = 0;
+    const __nv_bfloat16* src = base;
+    if (gr < n_valid) {
+      const int rem = d_valid - c * 8;
+      bytes = rem >= 8 ? 16 : (rem > 0 ? rem * 2 : 0);
+      if (bytes > 0) src = base + static_cast<int64_t>(gr) * row_stride + c * 8;
+    }
+    cp_async16(tile + swz(r, c), src, bytes);
+  }
+}
+
+// ---------------------------------------------------------------- forward
+struct AttnFwdParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  __nv_bfloat16* o;
+  float* lse;  // [BH, Nq] or null
+  Layout3 lq, lk, lv, lo;
+  int BH, Nq, Nk, d_valid;  // d_valid: true head dim (<= 64) of the output
+  int q_d_valid;            // columns of Q / K / V to read (<= 64)
+  float scale_log2;         // softmax scale * log2(e)
+};
+
+__global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwdParams p) {
+  __shared__ __align__(128) uint8_t sq[kBlkQ * 128];
+  __shared__ __align__(128) uint8_t sk[2][kBlkK * 128];
+  __shared__ __align__(128) uint8_t sv[2][kBlkK * 128];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t bh = blockIdx.y;
+  const int q0 = blockIdx.x * kBlkQ;
+  const __nv_bfloat16* qb = p.q + p.lq.offset(bh, 0);
+  const __nv_bfloat16* kb = p.k + p.lk.offset(bh, 0);
+  const __nv_bfloat16* vb = p.v + p.lv.offset(bh, 0);
+
+  load_tile(sq, qb, p.lq.row, q0, p.Nq, p.q_d_valid, tid, kAttnThreads);
+  load_tile(sk[0], kb, p.lk.row, 0, p.Nk, p.q_d_valid, tid, kAttnThreads);
+  load_tile(sv[0], vb, p.lv.row, 0, p.Nk, p.q_d_valid, tid, kAttnThreads);
+  cp_async_commit();
+
+  const int n_tiles = (p.Nk + kBlkK - 1) / kBlkK;
+  uint32_t qf[4][4];
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+  for (int t = 0; t < n_tiles; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < n_tiles) {
+      load_tile(sk[buf ^ 1], kb, p.lk.row, (t + 1) * kBlkK, p.Nk, p.q_d_valid, tid, kAttnThreads);
+      load_tile(sv[buf ^ 1], vb, p.lv.row, (t + 1) * kBlkK, p.Nk, p.q_d_valid, tid, kAttnThreads);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    if (t == 0) {
+      // Q fragments: rows warp*16 .. +15, k chunks of 16 columns
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int r = warp * 16 + (lane & 15);
+        const int c = kk * 2 + (lane >> 4);
+        ldsm_x4(qf[kk], smem_u32(sq + swz(r, c)));
+      }
+    }
+    // S = Q K^T : 16 x 64 per warp
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int j2 = 0; j2 < 4; ++j2) {
+        // two key n-tiles (16 keys) x 16 d: matrices (keys 0-7, d lo), (keys 0-7, d hi), (keys 8-15, d lo), (8-15, d hi)
+        uint32_t b[4];
+        const int key = j2 * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int c = kk * 2 + ((lane >> 3) & 1);
+        ldsm_x4(b, smem_u32(sk[buf] + swz(key, c)));
+        mma16816(s[2 * j2], qf[kk], b[0], b[1]);
+        mma16816(s[2 * j2 + 1], qf[kk], b[2], b[3]);
+      }
+    }
+    // mask keys beyond Nk
+    const int kbase = t * kBlkK;
+    if (kbase + kBlkK > p.Nk) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c0 = kbase + j * 8 + (lane & 3) * 2;
+        if (c0 >= p.Nk) s[j][0] = s[j][2] = -INFINITY;
+        if (c0 + 1 >= p.Nk) s[j][1] = s[j][3] = -INFINITY;
+      }
+    }
+    // online softmax (rows g and g+8 of the warp's 16)
+    float mx0 = m0, mx1 = m1;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]) * p.scale_log2);
+      mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]) * p.scale_log2);
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float a0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - mx0);
+    const float a1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - mx1);
+    const float mb0 = (mx0 == -INFINITY) ? 0.f : mx0;
+    const float mb1 = (mx1 == -INFINITY) ? 0.f : mx1;
+    m0 = mx0;
+    m1 = mx1;
+    float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      s[j][0] = exp2f(s[j][0] * p.scale_log2 - mb0);
+      s[j][1] = exp2f(s[j][1] * p.scale_log2 - mb0);
+      s[j][2] = exp2f(s[j][2] * p.scale_log2 - mb1);
+      s[j][3] = exp2f(s[j][3] * p.scale_log2 - mb1);
+      rs0 += s[j][0] + s[j][1];
+      rs1 += s[j][2] + s[j][3];
+    }
+    l0 = l0 * a0 + rs0;
+    l1 = l1 * a1 + rs1;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      o[i][0] *= a0;
+      o[i][1] *= a0;
+      o[i][2] *= a1;
+      o[i][3] *= a1;
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int i2 = 0; i2 < 4; ++i2) {
+        // V^T fragments: keys kk*16.., d columns i2*16.. ; trans load
+        uint32_t b[4];
+        const int key = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        const int c = i2 * 2 + (lane >> 4);
+        ldsm_x4_t(b, smem_u32(sv[buf] + swz(key, c)));
+        mma16816(o[2 * i2], pa, b[0], b[1]);
+        mma16816(o[2 * i2 + 1], pa, b[2], b[3]);
+      }
+    }
+    __syncthreads();
+  }
+  // finalize
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
+  const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  const int r0 = q0 + warp * 16 + (lane >> 2);
+  const int r1 = r0 + 8;
+  __nv_bfloat16* ob = p.o + p.lo.offset(bh, 0);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c = i * 8 + (lane & 3) * 2;
+    if (c < p.d_valid) {
+      if (r0 < p.Nq)
+        *reinterpret_cast<uint32_t*>(ob + static_cast<int64_t>(r0) * p.lo.row + c) =
+            pack_bf16x2(o[i][0] * inv0, o[i][1] * inv0);
+      if (r1 < p.Nq)
+        *reinterpret_cast<uint32_t*>(ob + static_cast<int64_t>(r1) * p.lo.row + c) =
+            pack_bf16x2(o[i][2] * inv1, o[i][3] * inv1);
+    }
+  }
+  if (p.lse != nullptr && (lane & 3) == 0) {
+    constexpr float kLn2 = 0.6931471805599453f;
+    if (r0 < p.Nq) p.lse[bh * p.Nq + r0] = l0 > 0.f ? (m0 + log2f(l0)) * kLn2 : -INFINITY;
+    if (r1 < p.Nq) p.lse[bh * p.Nq + r1] = l1 > 0.f ? (m1 + log2f(l1)) * kLn2 : -INFINITY;
+  }
+}
+
+// ---------------------------------------------------------------- backward
+// Dvec[bh, i] = sum_d dO[i, d] * O[i, d]
+__global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                                    Layout3 lo, Layout3 ldo, int BH, int Nq, int d_valid, float* __restrict__ dvec) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (idx >= static_cast<int64_t>(BH) * Nq) return;
+  const int64_t bh = idx / Nq;
+  const int r = static_cast<int>(idx % Nq);
+  const __nv_bfloat16* op = o + lo.offset(bh, r);
+  const __nv_bfloat16* dp = dout + ldo.offset(bh, r);
+  float s = 0.f;
+  for (int c = lane * 2; c < d_valid; c += 64) {
+    const uint32_t a = *reinterpret_cast<const uint32_t*>(op + c);
+    const uint32_t b = *reinterpret_cast<const uint32_t*>(dp + c);
+    s += bf16lo(a) * bf16lo(b) + bf16hi(a) * bf16hi(b);
+  }
+  s = warp_sum(s);
+  if (lane == 0) dvec[idx] = s;
+}
+
+struct AttnBwdParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const __nv_bfloat16* dout;
+  const float* lse;
+  const float* dvec;
+  float* dq;  // fp32 [BH, Nq, 64]
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  Layout3 lq, lk, lv, ldo, ldk, ldv;
+  int BH, Nq, Nk, d_valid, q_d_valid;
+  float scale, scale_log2;
+};
+
+__global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(AttnBwdParams p) {
+  __shared__ __align__(128) uint8_t sk[kBlkK * 128];
+  __shared__ __align__(128) uint8_t sv[kBlkK * 128];
+  __shared__ __align__(128) uint8_t sq[kBlkQ * 128];
+  __shared__ __align__(128) uint8_t sdo[kBlkQ * 128];
+  __shared__ __align__(128) uint8_t sds[kBlkK * 128];  // dS^T [key][q]
+  __shared__ float slse[kBlkQ], sdv[kBlkQ];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t bh = blockIdx.y;
+  const int k0 = blockIdx.x * kBlkK;
+  const __nv_bfloat16* qb = p.q + p.lq.offset(bh, 0);
+  const __nv_bfloat16* kb = p.k + p.lk.offset(bh, 0);
+  const __nv_bfloat16* vb = p.v + p.lv.offset(bh, 0);
+  const __nv_bfloat16* dob = p.dout + p.ldo.offset(bh, 0);
+
+  load_tile(sk, kb, p.lk.row, k0, p.Nk, p.q_d_valid, tid, kAttnThreads);
+  load_tile(sv, vb, p.lv.row, k0, p.Nk, p.q_d_valid, tid, kAttnThreads);
+  cp_async_commit();
+
+  float dk[8][4], dv[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dk[i][e] = dv[i][e] = 0.f;
+
+  uint32_t kf[4][4], vf[4][4];
+  const int n_qt = (p.Nq + kBlkQ - 1) / kBlkQ;
+  for (int qt = 0; qt < n_qt; ++qt) {
+    const int q0 = qt * kBlkQ;
+    load_tile(sq, qb, p.lq.row, q0, p.Nq, p.q_d_valid, tid, kAttnThreads);
+    load_tile(sdo, dob, p.ldo.row, q0, p.Nq, p.d_valid, tid, kAttnThreads);
+    cp_async_commit();
+    if (tid < kBlkQ) {
+      const int r = q0 + tid;
+      slse[tid] = r < p.Nq ? p.lse[bh * p.Nq + r] : INFINITY;
+      sdv[tid] = r < p.Nq ? p.dvec[bh * p.Nq + r] : 0.f;
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    if (qt == 0) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int r = warp * 16 + (lane & 15);
+        const int c = kk * 2 + (lane >> 4);
+        ldsm_x4(kf[kk], smem_u32(sk + swz(r, c)));
+        ldsm_x4(vf[kk], smem_u32(sv + swz(r, c)));
+      }
+    }
+    // S^T = K Q^T (16 keys x 64 q) and dP^T = V dO^T
+    float st[8][4], dpt[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) st[j][e] = dpt[j][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int j2 = 0; j2 < 4; ++j2) {
+        uint32_t b[4];
+        const int qr = j2 * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int c = kk * 2 + ((lane >> 3) & 1);
+        ldsm_x4(b, smem_u32(sq + swz(qr, c)));
+        mma16816(st[2 * j2], kf[kk], b[0], b[1]);
+        mma16816(st[2 * j2 + 1], kf[kk], b[2], b[3]);
+        ldsm_x4(b, smem_u32(sdo + swz(qr, c)));
+        mma16816(dpt[2 * j2], vf[kk], b[0], b[1]);
+        mma16816(dpt[2 * j2 + 1], vf[kk], b[2], b[3]);
+      }
+    }
+    // P^T and dS^T ; rows = keys (g, g+8 of the warp's 16), columns = queries
+    const int key0 = k0 + warp * 16 + (lane >> 2);
+    constexpr float kLog2e = 1.4426950408889634f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int qc = j * 8 + (lane & 3) * 2 + (e & 1);
+        const int key = key0 + ((e >> 1) << 3);
+        float pv = 0.f;
+        if (key < p.Nk && q0 + qc < p.Nq) pv = exp2f(st[j][e] * p.scale_log2 - slse[qc] * kLog2e);
+        st[j][e] = pv;
+        dpt[j][e] = pv * (dpt[j][e] - sdv[qc]);
+      }
+    }
+    // dV += P^T dO ; dK += dS^T Q  (A from registers; B = dO / Q with trans loads)
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t pa[4], da[4];
+      pa[0] = pack_bf16x2(st[2 * kk][0], st[2 * kk][1]);
+      pa[1] = pack_bf16x2(st[2 * kk][2], st[2 * kk][3]);
+      pa[2] = pack_bf16x2(st[2 * kk + 1][0], st[2 * kk + 1][1]);
+      pa[3] = pack_bf16x2(st[2 * kk + 1][2], st[2 * kk + 1][3]);
+      da[0] = pack_bf16x2(dpt[2 * kk][0], dpt[2 * kk][1]);
+      da[1] = pack_bf16x2(dpt[2 * kk][2], dpt[2 * kk][3]);
+      da[2] = pack_bf16x2(dpt[2 * kk + 1][0], dpt[2 * kk + 1][1]);
+      da[3] = pack_bf16x2(dpt[2 * kk + 1][2], dpt[2 * kk + 1][3]);
+#pragma unroll
+      for (int i2 = 0; i2 < 4; ++i2) {
+        uint32_t b[4];
+        const int qr = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        const int c = i2 * 2 + (lane >> 4);
+        ldsm_x4_t(b, smem_u32(sdo + swz(qr, c)));
+        mma16816(dv[2 * i2], pa, b[0], b[1]);
+        mma16816(dv[2 * i2 + 1], pa, b[2], b[3]);
+        ldsm_x4_t(b, smem_u32(sq + swz(qr, c)));
+        mma16816(dk[2 * i2], da, b[0], b[1]);
+        mma16816(dk[2 * i2 + 1], da, b[2], b[3]);
+      }
+    }
+    // dS^T -> shared (bf16, [key][q]) for the dQ product
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int qc = j * 8 + (lane & 3) * 2;
+      const int kr = warp * 16 + (lane >> 2);
+      *reinterpret_cast<uint32_t*>(sds + swz(kr, qc >> 3) + (qc & 7) * 2) = pack_bf16x2(dpt[j][0], dpt[j][1]);
+      *reinterpret_cast<uint32_t*>(sds + swz(kr + 8, qc >> 3) + (qc & 7) * 2) = pack_bf16x2(dpt[j][2], dpt[j][3]);
+    }
+    __syncthreads();
+    // dQ[q rows warp*16..] += dS (q x keys) K (keys x d) * scale ; A = dS via trans load of dS^T
+    {
+      float dqa[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dqa[i][0] = dqa[i][1] = dqa[i][2] = dqa[i][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t a[4];
+        // A[q][key] = dS^T[key][q]: matrices (q 0-7,key 0-7),(q 8-15,key 0-7),(q 0-7,key 8-15),(q 8-15,key 8-15)
+        {
+          const int key = kk * 16 + (lane & 7) + ((lane >> 4) << 3);
+          const int qcol = warp * 16 + (((lane >> 3) & 1) << 3);
+          ldsm_x4_t(a, smem_u32(sds + swz(key, qcol >> 3)));
+        }
+#pragma unroll
+        for (int i2 = 0; i2 < 4; ++i2) {
+          uint32_t b[4];
+          const int key = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+          const int c = i2 * 2 + (lane >> 4);
+          ldsm_x4_t(b, smem_u32(sk + swz(key, c)));
+          mma16816(dqa[2 * i2], a, b[0], b[1]);
+          mma16816(dqa[2 * i2 + 1], a, b[2], b[3]);
+        }
+      }
+      const int r0 = q0 + warp * 16 + (lane >> 2);
+      float* dqb = p.dq + bh * static_cast<int64_t>(p.Nq) * kD;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = i * 8 + (lane & 3) * 2;
+        if (r0 < p.Nq) {
+          atomicAdd(dqb + static_cast<int64_t>(r0) * kD + c, dqa[i][0] * p.scale);
+          atomicAdd(dqb + static_cast<int64_t>(r0) * kD + c + 1, dqa[i][1] * p.scale);
+        }
+        if (r0 + 8 < p.Nq) {
+          atomicAdd(dqb + static_cast<int64_t>(r0 + 8) * kD + c, dqa[i][2] * p.scale);
+          atomicAdd(dqb + static_cast<int64_t>(r0 + 8) * kD + c + 1, dqa[i][3] * p.scale);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // write dK (scaled), dV
+  const int r0 = k0 + warp * 16 + (lane >> 2);
+  __nv_bfloat16* dkb = p.dk + p.ldk.offset(bh, 0);
+  __nv_bfloat16* dvb = p.dv + p.ldv.offset(bh, 0);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c = i * 8 + (lane & 3) * 2;
+    if (c >= p.d_valid) continue;
+    if (r0 < p.Nk) {
+      *reinterpret_cast<uint32_t*>(dkb + static_cast<int64_t>(r0) * p.ldk.row + c) =
+          pack_bf16x2(dk[i][0] * p.scale, dk[i][1] * p.scale);
+      *reinterpret_cast<uint32_t*>(dvb + static_cast<int64_t>(r0) * p.ldv.row + c) = pack_bf16x2(dv[i][0], dv[i][1]);
+    }
+    if (r0 + 8 < p.Nk) {
+      *reinterpret_cast<uint32_t*>(dkb + static_cast<int64_t>(r0 + 8) * p.ldk.row + c) =
+          pack_bf16x2(dk[i][2] * p.scale, dk[i][3] * p.scale);
+      *reinterpret_cast<uint32_t*>(dvb + static_cast<int64_t>(r0 + 8) * p.ldv.row + c) =
+          pack_bf16x2(dv[i][2], dv[i][3]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- host
+static Layout3 to_layout(const std::vector<int64_t>& l) {
+  TORCH_CHECK(l.size() == 6, "layout: [s0, s1, s2, row, d1, d2] expected");
+  return Layout3{l[0], l[1], l[2], l[3], static_cast<int>(l[4]), static_cast<int>(l[5])};
+}
+
+static void check_bf16(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, ": bf16 CUDA tensor expected");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, ": 16-byte aligned base expected");
+}
+
+// q/k/v/o are base tensors (any shape); the layouts give element strides relative to their data_ptr.
+void attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
+              const c10::optional<torch::Tensor>& lse, std::vector<int64_t> lq, std::vector<int64_t> lk,
+              std::vector<int64_t> lv, std::vector<int64_t> lo, int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid,
+              double scale) {
+  check_bf16(q, "q");
+  check_bf16(k, "k");
+  check_bf16(v, "v");
+  check_bf16(o, "o");
+  TORCH_CHECK(d_valid > 0 && d_valid <= kD && d_valid % 8 == 0, "attn_fwd: head dim must be a multiple of 8, <= 64");
+  const at::cuda::CUDAGuard guard(q.device());
+  AttnFwdParams p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  p.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.lq = to_layout(lq);
+  p.lk = to_layout(lk);
+  p.lv = to_layout(lv);
+  p.lo = to_layout(lo);
+  TORCH_CHECK(p.lq.row % 8 == 0 && p.lk.row % 8 == 0 && p.lv.row % 8 == 0 && p.lq.s0 % 8 == 0 && p.lq.s1 % 8 == 0 &&
+                  p.lq.s2 % 8 == 0 && p.lk.s0 % 8 == 0 && p.lk.s1 % 8 == 0 && p.lk.s2 % 8 == 0 &&
+                  p.lv.s0 % 8 == 0 && p.lv.s1 % 8 == 0 && p.lv.s2 % 8 == 0,
+              "attn_fwd: Q/K/V rows must start on 16-byte boundaries");
+  p.BH = static_cast<int>(BH);
+  p.Nq = static_cast<int>(Nq);
+  p.Nk = static_cast<int>(Nk);
+  p.d_valid = static_cast<int>(d_valid);
+  p.q_d_valid = p.d_valid;
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  if (lse.has_value() && lse->defined()) {
+    TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->numel() >= BH * Nq, "attn_fwd: fp32 lse [BH, Nq]");
+    p.lse = lse->data_ptr<float>();
+  }
+  if (BH == 0 || Nq == 0) return;
+  TORCH_CHECK(Nk > 0, "attn_fwd: at least one key");
+  TORCH_CHECK(BH < 65536 * 32768LL, "attn_fwd: too many heads");
+  dim3 grid(static_cast<unsigned>((Nq + kBlkQ - 1) / kBlkQ), static_cast<unsigned>(BH));
+  TORCH_CHECK(BH <= 2147483647LL, "attn_fwd: BH too large");
+  attn_fwd_kernel<<<grid, kAttnThreads, 0, at::cuda::getCurrentCUDAStream()>>>(p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& o,
+              const torch::Tensor& dout, const torch::Tensor& lse, torch::Tensor& dq, torch::Tensor& dk,
+              torch::Tensor& dv, std::vector<int64_t> lq, std::vector<int64_t> lk, std::vector<int64_t> lv,
+              std::vector<int64_t> lo, std::vector<int64_t> ldo, std::vector<int64_t> ldk, std::vector<int64_t> ldv,
+              int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid, double scale) {
+  for (auto* t : std::initializer_list<const torch::Tensor*>{&q, &k, &v, &o, &dout, &dk, &dv}) check_bf16(*t, "attn_bwd");
+  TORCH_CHECK(dq.scalar_type() == at::kFloat && dq.is_contiguous() && dq.numel() == BH * Nq * kD,
+              "attn_bwd: dq must be a zeroed fp32 [BH, Nq, 64] accumulator");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() >= BH * Nq, "attn_bwd: fp32 lse");
+  TORCH_CHECK(d_valid > 0 && d_valid <= kD && d_valid % 8 == 0, "attn_bwd: head dim must be a multiple of 8, <= 64");
+  const at::cuda::CUDAGuard guard(q.device());
+  if (BH == 0 || Nq == 0 || Nk == 0) return;
+  auto dvec = torch::empty({BH * Nq}, lse.options());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  {
+    const int64_t rows = BH * Nq;
+    attn_bwd_dot_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+        to_layout(lo), to_layout(ldo), static_cast<int>(BH), static_cast<int>(Nq), static_cast<int>(d_valid),
+        dvec.data_ptr<float>());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  AttnBwdParams p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  p.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  p.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  p.lse = lse.data_ptr<float>();
+  p.dvec = dvec.data_ptr<float>();
+  p.dq = dq.data_ptr<float>();
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  p.lq = to_layout(lq);
+  p.lk = to_layout(lk);
+  p.lv = to_layout(lv);
+  p.ldo = to_layout(ldo);
+  p.ldk = to_layout(ldk);
+  p.ldv = to_layout(ldv);
+  p.BH = static_cast<int>(BH);
+  p.Nq = static_cast<int>(Nq);
+  p.Nk = static_cast<int>(Nk);
+  p.d_valid = static_cast<int>(d_valid);
+  p.q_d_valid = p.d_valid;
+  p.scale = static_cast<float>(scale);
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  dim3 grid(static_cast<unsigned>((Nk + kBlkK - 1) / kBlkK), static_cast<unsigned>(BH));
+  attn_bwd_kernel<<<grid, kAttnThreads, 0, stream>>>(p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace nori

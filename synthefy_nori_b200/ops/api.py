@@ -13,8 +13,9 @@ __all__ = [
     "gemm",
     "gemm_swiglu",
     "gemm_residual",
-    "gemm_f32",
-    "gemm_headmajor",
+    "gemm_wgrad",
+    "attention_fwd",
+    "attention_bwd",
     "rms_scale",
     "sumsq_to_scale",
     "pinball_loss_grad",
@@ -22,6 +23,7 @@ __all__ = [
     "adamw_ema_step",
     "quantize_int8",
     "status_word",
+    "check_status",
     "interleave_swiglu_weights",
 ]
 
@@ -50,9 +52,12 @@ def check_status(device: torch.device) -> None:
         raise RuntimeError(f"native kernel reported a bounded-wait timeout (status code {code})")
 
 
-def gemm(a: torch.Tensor, w: torch.Tensor, row_scale=None, bias=None, bn: int = 0) -> torch.Tensor:
-    """bf16 ``(a @ w.T) * row_scale[:, None] + bias`` on tcgen05 (fp32 accumulation)."""
-    return _lib().gemm_bf16(a, w, row_scale, bias, status_word(a.device), bn)
+def gemm(a: torch.Tensor, w: torch.Tensor, row_scale=None, bias=None, bn: int = 0, w_kn: bool = False) -> torch.Tensor:
+    """bf16 ``(a @ W.T) * row_scale[:, None] + bias`` on tcgen05 (fp32 accumulation).
+
+    ``w`` is ``W`` [N, K], or with ``w_kn=True`` the same matrix stored as [K, N]
+    (so ``gemm(dy, W, w_kn=True)`` is the input gradient ``dy @ W``)."""
+    return _lib().gemm_bf16(a, w, row_scale, bias, status_word(a.device), bn, w_kn)
 
 
 def gemm_swiglu(a: torch.Tensor, w_interleaved: torch.Tensor, row_scale=None, bn: int = 0) -> torch.Tensor:
@@ -65,16 +70,31 @@ def gemm_residual(a, w, resid, alpha: float, sumsq=None, bn: int = 0) -> torch.T
     return _lib().gemm_residual(a, w, resid, float(alpha), sumsq, status_word(a.device), bn)
 
 
-def gemm_f32(a, w, out=None, accumulate: bool = False, bn: int = 0) -> torch.Tensor:
-    if out is None:
-        out = torch.empty(a.shape[0], w.shape[0], device=a.device, dtype=torch.float32)
-    _lib().gemm_f32_out(a, w, out, accumulate, status_word(a.device), bn)
+def gemm_wgrad(dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor, bn: int = 0, splits: int = 0) -> torch.Tensor:
+    """``out += dy.T @ x`` in fp32 (weight gradient; split over tokens)."""
+    _lib().gemm_wgrad(dy, x, out, status_word(dy.device), bn, splits)
     return out
 
 
-def gemm_headmajor(a, w, out, *, T, n_rows, J, H, D, Dp, row_scale=None, bn: int = 0):
-    _lib().gemm_headmajor(a, w, row_scale, out, T, n_rows, J, H, D, Dp, status_word(a.device), bn)
-    return out
+def _layout(l):
+    return [int(v) for v in l]
+
+
+def attention_fwd(q, k, v, o, *, lq, lk, lv, lo, BH, Nq, Nk, d, scale, lse=None):
+    """Flash attention forward over strided views. Each layout is
+    ``(s0, s1, s2, row_stride, d1, d2)``: head index ``bh`` decomposes as
+    ``i2 = bh % d2, i1 = (bh // d2) % d1, i0 = bh // (d1 * d2)`` and row ``r`` of head
+    ``bh`` starts at element ``i0*s0 + i1*s1 + i2*s2 + r*row_stride`` of the tensor."""
+    _lib().attn_fwd(q, k, v, o, lse, _layout(lq), _layout(lk), _layout(lv), _layout(lo), int(BH), int(Nq), int(Nk),
+                    int(d), float(scale))
+    return o
+
+
+def attention_bwd(q, k, v, o, do, lse, dq_f32, dk, dv, *, lq, lk, lv, lo, ldo, ldk, ldv, BH, Nq, Nk, d, scale):
+    """Flash attention backward. ``dq_f32`` is a zeroed fp32 [BH, Nq, 64] accumulator
+    (scaled dQ); dK / dV are written through their layouts."""
+    _lib().attn_bwd(q, k, v, o, do, lse, dq_f32, dk, dv, _layout(lq), _layout(lk), _layout(lv), _layout(lo),
+                    _layout(ldo), _layout(ldk), _layout(ldv), int(BH), int(Nq), int(Nk), int(d), float(scale))
 
 
 def rms_scale(x: torch.Tensor, eps: float) -> torch.Tensor:

@@ -1,0 +1,87 @@
+"""Flash attention kernels vs an fp32 PyTorch reference (forward and backward), on the
+token-major strided layouts the encoder uses."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from synthefy_nori_b200 import ops  # noqa: E402
+
+
+def _ref_attn(q, k, v, scale):
+    s = torch.einsum("bqd,bkd->bqk", q.float(), k.float()) * scale
+    p = torch.softmax(s, -1)
+    return torch.einsum("bqk,bkd->bqd", p, v.float()), torch.logsumexp(s, -1)
+
+
+@pytest.mark.parametrize("BH,Nq,Nk", [(3, 64, 64), (5, 100, 37), (2, 51, 51), (4, 300, 700), (1, 1, 1)])
+def test_headmajor_fwd_bwd(BH, Nq, Nk):
+    torch.manual_seed(0)
+    D = 56
+    scale = 1 / math.sqrt(D)
+    q = torch.zeros(BH, Nq, 64, device="cuda", dtype=torch.bfloat16)
+    k = torch.zeros(BH, Nk, 64, device="cuda", dtype=torch.bfloat16)
+    v = torch.zeros(BH, Nk, 64, device="cuda", dtype=torch.bfloat16)
+    q[..., :D] = torch.randn(BH, Nq, D, device="cuda").to(torch.bfloat16)
+    k[..., :D] = torch.randn(BH, Nk, D, device="cuda").to(torch.bfloat16)
+    v[..., :D] = torch.randn(BH, Nk, D, device="cuda").to(torch.bfloat16)
+    o = torch.empty(BH, Nq, D, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(BH, Nq, device="cuda")
+    hm = lambda n: (n * 64, 0, 0, 64, 1, 1)  # noqa: E731
+    ops.attention_fwd(q, k, v, o, lq=hm(Nq), lk=hm(Nk), lv=hm(Nk), lo=(Nq * D, 0, 0, D, 1, 1), BH=BH, Nq=Nq, Nk=Nk,
+                      d=D, scale=scale, lse=lse)
+    qf = q[..., :D].float().requires_grad_(True)
+    kf = k[..., :D].float().requires_grad_(True)
+    vf = v[..., :D].float().requires_grad_(True)
+    ref, ref_lse = _ref_attn(qf, kf, vf, scale)
+    torch.testing.assert_close(o.float(), ref.detach(), atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(lse, ref_lse.detach(), atol=1e-3, rtol=1e-3)
+    do = torch.randn(BH, Nq, D, device="cuda").to(torch.bfloat16)
+    ref.backward(do.float())
+    dq = torch.zeros(BH, Nq, 64, device="cuda")
+    dk = torch.empty(BH, Nk, D, device="cuda", dtype=torch.bfloat16)
+    dv = torch.empty(BH, Nk, D, device="cuda", dtype=torch.bfloat16)
+    tm = lambda n: (n * D, 0, 0, D, 1, 1)  # noqa: E731
+    ops.attention_bwd(q, k, v, o, do, lse, dq, dk, dv, lq=hm(Nq), lk=hm(Nk), lv=hm(Nk), lo=tm(Nq), ldo=tm(Nq), ldk=tm(Nk),
+                      ldv=tm(Nk), BH=BH, Nq=Nq, Nk=Nk, d=D, scale=scale)
+    torch.testing.assert_close(dq[..., :D], qf.grad, atol=5e-2, rtol=5e-2)
+    torch.testing.assert_close(dk.float(), kf.grad, atol=5e-2, rtol=5e-2)
+    torch.testing.assert_close(dv.float(), vf.grad, atol=5e-2, rtol=5e-2)
+    assert dq[..., D:].abs().max().item() == 0
+
+
+def test_token_major_sequence_and_feature_layouts():
+    """Sequence attention over rows n per (b, t, h) and feature attention over tokens t
+    per (b, n, h), both read straight from one token-major QKV buffer [B, N, T, 3, H, D]."""
+    torch.manual_seed(1)
+    B, N, T, H, D = 2, 90, 9, 2, 56
+    qkv = torch.randn(B, N, T, 3, H, D, device="cuda").to(torch.bfloat16)
+    scale = 1 / math.sqrt(D)
+    E3 = 3 * H * D
+    # sequence attention: bh = (b*T + t)*H + h
+    out = torch.empty(B, N, T, H, D, device="cuda", dtype=torch.bfloat16)
+    lay = (N * T * E3, E3, D, T * E3, T, H)
+    ops.attention_fwd(qkv[..., 0, :, :], qkv[..., 1, :, :], qkv[..., 2, :, :], out, lq=lay, lk=lay, lv=lay,
+                      lo=(N * T * H * D, H * D, D, T * H * D, T, H), BH=B * T * H, Nq=N, Nk=N, d=D, scale=scale)
+    q = qkv[..., 0, :, :].permute(0, 1, 3, 2, 4)  # B N H T D? build reference explicitly
+    qs = qkv[:, :, :, 0].permute(0, 2, 3, 1, 4).reshape(B * T * H, N, D)
+    ks = qkv[:, :, :, 1].permute(0, 2, 3, 1, 4).reshape(B * T * H, N, D)
+    vs = qkv[:, :, :, 2].permute(0, 2, 3, 1, 4).reshape(B * T * H, N, D)
+    ref, _ = _ref_attn(qs, ks, vs, scale)
+    ref = ref.view(B, T, H, N, D).permute(0, 3, 1, 2, 4)
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
+    # feature attention: bh = (b*N + n)*H + h, rows t
+    out2 = torch.empty(B, N, T, H, D, device="cuda", dtype=torch.bfloat16)
+    lay2 = (T * E3, 0, D, E3, 1, H)
+    ops.attention_fwd(qkv[..., 0, :, :], qkv[..., 1, :, :], qkv[..., 2, :, :], out2, lq=lay2, lk=lay2, lv=lay2,
+                      lo=(T * H * D, 0, D, H * D, 1, H), BH=B * N * H, Nq=T, Nk=T, d=D, scale=scale)
+    qf = qkv[:, :, :, 0].permute(0, 1, 3, 2, 4).reshape(B * N * H, T, D)
+    kf = qkv[:, :, :, 1].permute(0, 1, 3, 2, 4).reshape(B * N * H, T, D)
+    vf = qkv[:, :, :, 2].permute(0, 1, 3, 2, 4).reshape(B * N * H, T, D)
+    ref2, _ = _ref_attn(qf, kf, vf, scale)
+    ref2 = ref2.view(B, N, H, T, D).permute(0, 1, 3, 2, 4)
+    torch.testing.assert_close(out2.float(), ref2, atol=2e-2, rtol=2e-2)
+    del q

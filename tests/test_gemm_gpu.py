@@ -17,7 +17,7 @@ def _rand(*shape, scale=1.0):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (300, 448, 448), (1000, 1344, 448), (257, 96, 128), (4096, 896, 896), (77, 352, 352)])
-@pytest.mark.parametrize("bn", [0, 128, 256])
+@pytest.mark.parametrize("bn", [0, 128, 192, 256])
 def test_gemm_plain(M, N, K, bn):
     torch.manual_seed(0)
     a, w = _rand(M, K), _rand(N, K, scale=K ** -0.5)
@@ -62,24 +62,21 @@ def test_gemm_residual(M, N, K):
     torch.testing.assert_close(ssq, (out.float() ** 2).sum(1), atol=1e-2, rtol=1e-3)
 
 
-def test_gemm_f32_accumulate():
+@pytest.mark.parametrize("M,N,K", [(1000, 448, 1344), (300, 896, 448), (129, 128, 256)])
+def test_gemm_dgrad_w_kn(M, N, K):
+    """dX = dY @ W with W [N_in... stored [K, N]]: B operand read MN-major."""
     torch.manual_seed(4)
-    a, w = _rand(300, 256), _rand(200, 256)
-    out = torch.randn(300, 200, device="cuda")
-    ref = out + _ref(a, w)
-    ops.gemm_f32(a, w, out, accumulate=True)
-    torch.testing.assert_close(out, ref, atol=2e-2, rtol=1e-3)
+    dy = _rand(M, K)
+    w = _rand(K, N, scale=K ** -0.5)  # W stored [K, N]
+    out = ops.gemm(dy, w, w_kn=True)
+    torch.testing.assert_close(out.float(), dy.float() @ w.float(), atol=3e-2, rtol=3e-2)
 
 
-def test_gemm_headmajor():
+@pytest.mark.parametrize("T,No,Ki", [(5000, 448, 448), (777, 1344, 448), (64, 128, 256)])
+def test_gemm_wgrad(T, No, Ki):
     torch.manual_seed(5)
-    B, n, T, H, D, Dp = 2, 37, 5, 2, 56, 64
-    E = 112
-    a = _rand(B * n * T, E)
-    w = _rand(3 * H * D, E, scale=E ** -0.5)
-    out = torch.zeros(B * T * 3 * H * n * Dp, device="cuda", dtype=torch.bfloat16)
-    ops.gemm_headmajor(a, w, out, T=T, n_rows=n, J=3, H=H, D=D, Dp=Dp)
-    ref = _ref(a, w).view(B, n, T, 3, H, D).permute(0, 2, 3, 4, 1, 5)  # B T J H n D
-    got = out.view(B, T, 3, H, n, Dp)
-    torch.testing.assert_close(got[..., :D].float(), ref, atol=2e-2, rtol=2e-2)
-    assert got[..., D:].abs().max().item() == 0
+    dy, x = _rand(T, No, scale=0.1), _rand(T, Ki)
+    out = torch.randn(No, Ki, device="cuda")
+    ref = out + dy.float().T @ x.float()
+    ops.gemm_wgrad(dy, x, out)
+    torch.testing.assert_close(out, ref, atol=5e-2, rtol=1e-2)
