@@ -7,6 +7,8 @@ and raises if the extension is missing on a GPU box: there is no silent fallback
 
 from __future__ import annotations
 
+import torch  # noqa: F401  (loads libc10 / libtorch before the extension)
+
 _C = None
 _IMPORT_ERROR: str | None = None
 
