@@ -1,0 +1,354 @@
+"""Headline benchmark: nori-100m DDP pretraining throughput (tables/s, whole job).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 run under ``torch.distributed.run`` (one rank per GPU, NCCL, rendezvous on
+127.0.0.1).  Config (nori-100m training on the config-3 table shapes):
+random-init nori-100m weights, synthetic SCM-prior tables, 32 tables per GPU per step,
+rows ~ U[512, 2048] (one row count per step, shared by the batch), context fraction
+~ U[0.5, 0.9], features ~ U[5, 100] padded to 100, 999-quantile pinball loss (+0.05
+monotonicity), bf16 compute, clip 1.0, AdamW + EMA 0.999, activation checkpointing.
+
+``value`` times W untimed warm-up steps then exactly K steps on the device (CUDA
+events, barrier + synchronize on both sides, max over ranks); each step generates its
+tables on the GPU, runs forward + backward, reduces gradients across ranks and applies
+the optimizer.  Every step's activations are several GB (far above the 126 MB L2), so
+no L2 flush is needed between steps.  ``e2e`` runs the same training through the
+public ``NoriTrainer.train_step`` with each step's tables copied host->device from
+pinned memory and the loss read back to the host.
+
+``--impl reference`` runs the unmodified reference package from ``baseline/_ref``
+(its FeaturesTransformer with bf16 autocast, SDPA attention, native RMSNorm, layer
+checkpointing, ``compute_ccmm_loss`` pinball objective, torch AdamW, its EMA helper,
+DDP/NCCL for N > 1) on the same table shapes; its tables are generated before the
+timed region.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "nori-100m train tables/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=6)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", default="nori-100m")
+    ap.add_argument("--tables-per-gpu", type=int, default=32)
+    ap.add_argument("--min-rows", type=int, default=512)
+    ap.add_argument("--max-rows", type=int, default=2048)
+    ap.add_argument("--features", type=int, default=100)
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--grad-reduction", default="nccl", choices=["nccl", "peer"])
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.proc = None
+        self.path = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            fd, self.path = tempfile.mkstemp(prefix="nori_clocks_", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200", "-i",
+                 ident], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        loaded = [s for s in sm if s > 0.5 * smax] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax, "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+# ----------------------------------------------------------------------------- shapes
+def step_shapes(args, n: int):
+    g = torch.Generator().manual_seed(args.seed)
+    out = []
+    for _ in range(n):
+        rows = int(torch.randint(args.min_rows, args.max_rows + 1, (1,), generator=g).item())
+        frac = 0.5 + 0.4 * float(torch.rand(1, generator=g).item())
+        ep = min(max(1, int(rows * frac)), rows - 1)
+        out.append((rows, ep))
+    return out
+
+
+def prior_cfg(args):
+    from synthefy_nori_b200.training.prior import PriorConfig
+
+    return PriorConfig(min_features=5, max_features=args.features, pad_features=args.features)
+
+
+def timed(fn_steps, device, world):
+    """Run fn_steps() between barriers; return max-over-ranks device milliseconds."""
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    fn_steps()
+    end.record()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    ms = torch.tensor([start.elapsed_time(end)], device=device)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    return float(ms.item())
+
+
+def count_native_launches(step_fn) -> int:
+    """Kernels of this repository's extension launched by one step (profiled, untimed)."""
+    from torch.profiler import ProfilerActivity, profile
+
+    names = ("nori::", "gemm_kernel", "attn_fwd_kernel", "attn_bwd", "rms_", "pinball_kernel", "adamw_ema_kernel",
+             "sumsq_kernel", "swiglu_bwd_kernel", "quant_int8_kernel", "peer_")
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    n = 0
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA and any(k in ev.name for k in names):
+            n += 1
+    return n
+
+
+# ----------------------------------------------------------------------------- arms
+def run_ours(args, device, world, rank):
+    from synthefy_nori_b200 import ops
+    from synthefy_nori_b200.models.config import preset_config
+    from synthefy_nori_b200.training.prior import scm_prior_batch
+    from synthefy_nori_b200.training.trainer import NoriTrainer, TrainConfig
+    from synthefy_nori_b200.utils.loading import build_model
+
+    if not ops.native_available():
+        raise RuntimeError(f"native extension not loaded: {ops.native_import_error()}")
+    torch.manual_seed(args.seed)
+    model = build_model(preset_config(args.model))
+    trainer = NoriTrainer(model, TrainConfig(grad_reduction=args.grad_reduction), device)
+    pc = prior_cfg(args)
+    B = args.tables_per_gpu
+    shapes = step_shapes(args, args.warmup + args.steps + 1)
+
+    def one(i):
+        rows, ep = shapes[i]
+        b = scm_prior_batch(pc, B, rows, ep, seed=args.seed * 1000003 + i * 7919 + rank, device=device)
+        return trainer.train_step(b.x, b.y, b.eval_pos)
+
+    for i in range(args.warmup):
+        one(i)
+    clocks = ClockSampler(device)
+    losses = []
+    ms = timed(lambda: [losses.append(one(args.warmup + i)) for i in range(args.steps)], device, world)
+    clk = clocks.stop()
+    launches = count_native_launches(lambda: one(args.warmup + args.steps)) * args.steps
+    ops.check_status(device)
+    e2e = None if args.no_e2e else run_e2e(args, trainer, shapes, device, world, rank)
+    return ms, clk, launches, e2e, float(losses[-1].item())
+
+
+def run_e2e(args, trainer, shapes, device, world, rank):
+    """Public-API training from pinned host tables: H2D copy + train_step + loss.item()."""
+    from synthefy_nori_b200.training.prior import scm_prior_batch
+
+    pc = prior_cfg(args)
+    B = args.tables_per_gpu
+    host = []
+    for i in range(args.steps + 1):
+        rows, ep = shapes[i]
+        b = scm_prior_batch(pc, B, rows, ep, seed=args.seed * 7 + i + 100 * rank, device=device)
+        host.append((b.x.cpu().pin_memory(), b.y.cpu().pin_memory(), ep))
+    torch.cuda.synchronize(device)
+
+    def one(i):
+        x_h, y_h, ep = host[i]
+        x = x_h.to(device, non_blocking=True)
+        y = y_h.to(device, non_blocking=True)
+        return float(trainer.train_step(x, y, ep).item())
+
+    one(args.steps)  # warm
+    ms = timed(lambda: [one(i) for i in range(args.steps)], device, world)
+    h2d = sum(host[i][0].numel() * 4 + host[i][1].numel() * 4 for i in range(args.steps)) / args.steps
+    tables = B * world * args.steps
+    return {"value": tables / (ms / 1000.0), "unit": "tables/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": 4, "ms_per_step": ms / args.steps}
+
+
+def run_reference(args, device, world, rank):
+    from synthefy_nori_b200.utils.reference import import_reference
+
+    if import_reference() is None:
+        return None
+    from synthefy_nori.model.layer import RMSNorm as RefRMSNorm
+    from synthefy_nori.training.loss import compute_ccmm_loss
+    from synthefy_nori.training.trainer import _foreach_ema_update
+    from synthefy_nori.utils.loading import build_model as ref_build
+
+    from synthefy_nori_b200.models.config import preset_config
+    from synthefy_nori_b200.training.prior import scm_prior_batch
+
+    torch.manual_seed(args.seed)
+    cfg = dict(preset_config(args.model))
+    cfg["mask_prediction"] = True  # the training CLI's setting (reference training/cli.py:1192)
+    model = ref_build(cfg).to(device)
+    for m in model.modules():  # native RMSNorm, as the training CLI enables (cli.py:1330-1342)
+        if isinstance(m, RefRMSNorm):
+            m.use_native = True
+    model._skip_feature_decoder = True  # feature loss weight 0 (cli.py:1344-1350)
+    model.transformer_encoder.gradient_checkpointing = True
+    model.train()
+    net = model
+    if world > 1:
+        from torch.nn.parallel import DistributedDataParallel as DDP
+
+        net = DDP(model, device_ids=[device.index], find_unused_parameters=False, gradient_as_bucket_view=True)
+    params = [p for p in model.parameters() if p.requires_grad]
+    opt = torch.optim.AdamW(params, lr=3e-4, betas=(0.9, 0.95), weight_decay=0.01)
+    ema = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    quantiles = list(model.regression_quantiles)
+    pc = prior_cfg(args)
+    B = args.tables_per_gpu
+    shapes = step_shapes(args, args.warmup + args.steps)
+    batches = []
+    for i, (rows, ep) in enumerate(shapes):
+        b = scm_prior_batch(pc, B, rows, ep, seed=args.seed * 1000003 + i * 7919 + rank, device=device)
+        batches.append((b.x, b.y, ep))
+
+    def one(i):
+        x, y, ep = batches[i]
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+            out = net(x=x, y=y[:, :ep], eval_pos=ep, task_type="reg")
+        loss, _ = compute_ccmm_loss(out, y[:, ep:], x, None, "reg", feature_loss_weight=0.0,
+                                    regression_loss="pinball", regression_quantiles=quantiles,
+                                    pinball_monotonicity_weight=0.05)
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(params, 1.0)
+        opt.step()
+        _foreach_ema_update(ema, model.state_dict(), 0.999)
+        return loss.detach()
+
+    for i in range(args.warmup):
+        one(i)
+    clocks = ClockSampler(device)
+    losses = []
+    ms = timed(lambda: [losses.append(one(args.warmup + i)) for i in range(args.steps)], device, world)
+    clk = clocks.stop()
+    return ms, clk, 0, None, float(losses[-1].item())
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    t0 = time.time()
+    if args.impl == "reference":
+        res = run_reference(args, device, world, rank)
+        if res is None:
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "reference package not installed under baseline/_ref"}))
+            return
+    else:
+        res = run_ours(args, device, world, rank)
+    ms, clk, launches, e2e, last_loss = res
+    tables = args.tables_per_gpu * world * args.steps
+    value = tables / (ms / 1000.0)
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": "tables/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (GPU SCM-prior tables, random-init weights)",
+            "config": {
+                "model": args.model,
+                "global_batch": args.tables_per_gpu * world,
+                "seq_len": f"rows U[{args.min_rows},{args.max_rows}] x {args.features} features (padded)",
+                "parallelism": f"dp{world}",
+                "tables_per_gpu": args.tables_per_gpu,
+                "loss": "pinball 999 + 0.05 monotonicity",
+                "optimizer": "AdamW + EMA 0.999, clip 1.0",
+                "l2": "per-step working set is several GB (> 126 MB L2); no flush needed",
+                "grad_reduction": args.grad_reduction if args.impl == "ours" else "DDP/NCCL",
+            },
+            "clocks": clk,
+            "gpu_launches": launches,
+            "last_loss": last_loss,
+            "wall_s": round(time.time() - t0, 1),
+        }
+        if args.impl == "reference":
+            line["impl"] = "reference"
+        if e2e is not None:
+            line["e2e"] = e2e
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

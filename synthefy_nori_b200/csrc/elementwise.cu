@@ -63,6 +63,136 @@ torch::Tensor rms_scale(const torch::Tensor& x, double eps) {
   return rs;
 }
 
+// xn = bf16(x * rs[row]); one warp per row.
+__global__ void rms_apply_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ rs, int64_t M, int E,
+                                 __nv_bfloat16* __restrict__ y) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= M) return;
+  const float r = rs[row];
+  const __nv_bfloat16* xr = x + row * E;
+  __nv_bfloat16* yr = y + row * E;
+  for (int c = lane * 8; c < E; c += 256) {
+    const uint4 w = *reinterpret_cast<const uint4*>(xr + c);
+    const uint32_t a[4] = {w.x, w.y, w.z, w.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = pack_bf16x2(bf16lo(a[i]) * r, bf16hi(a[i]) * r);
+    *reinterpret_cast<uint4*>(yr + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+torch::Tensor rms_apply(const torch::Tensor& x, const torch::Tensor& rs) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.is_contiguous() && x.size(1) % 8 == 0,
+              "rms_apply: contiguous bf16 [M, E] (E % 8 == 0)");
+  TORCH_CHECK(rs.scalar_type() == at::kFloat && rs.numel() == x.size(0), "rms_apply: fp32 rs [M]");
+  const at::cuda::CUDAGuard guard(x.device());
+  auto y = torch::empty_like(x);
+  const int64_t M = x.size(0);
+  if (M == 0) return y;
+  rms_apply_kernel<<<(M + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), rs.data_ptr<float>(), M, static_cast<int>(x.size(1)),
+      reinterpret_cast<__nv_bfloat16*>(y.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return y;
+}
+
+// RMSNorm (no affine) backward fused with the residual-gradient add:
+//   dx = dres + rs * dxn - x * rs^3 * mean(dxn * x)
+__global__ void rms_bwd_kernel(const __nv_bfloat16* __restrict__ dxn, const __nv_bfloat16* __restrict__ x,
+                               const float* __restrict__ rs, const __nv_bfloat16* __restrict__ dres, int64_t M, int E,
+                               __nv_bfloat16* __restrict__ dx) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= M) return;
+  const __nv_bfloat16* gr = dxn + row * E;
+  const __nv_bfloat16* xr = x + row * E;
+  float dot = 0.f;
+  for (int c = lane * 8; c < E; c += 256) {
+    const uint4 g = *reinterpret_cast<const uint4*>(gr + c);
+    const uint4 w = *reinterpret_cast<const uint4*>(xr + c);
+    const uint32_t ga[4] = {g.x, g.y, g.z, g.w}, xa[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dot += bf16lo(ga[i]) * bf16lo(xa[i]) + bf16hi(ga[i]) * bf16hi(xa[i]);
+  }
+  dot = warp_sum(dot);
+  const float r = rs[row];
+  const float coef = r * r * r * dot / static_cast<float>(E);
+  for (int c = lane * 8; c < E; c += 256) {
+    const uint4 g = *reinterpret_cast<const uint4*>(gr + c);
+    const uint4 w = *reinterpret_cast<const uint4*>(xr + c);
+    const uint32_t ga[4] = {g.x, g.y, g.z, g.w}, xa[4] = {w.x, w.y, w.z, w.w};
+    uint32_t da[4] = {0u, 0u, 0u, 0u};
+    if (dres != nullptr) {
+      const uint4 d = *reinterpret_cast<const uint4*>(dres + row * E + c);
+      da[0] = d.x; da[1] = d.y; da[2] = d.z; da[3] = d.w;
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float lo = bf16lo(da[i]) + r * bf16lo(ga[i]) - coef * bf16lo(xa[i]);
+      const float hi = bf16hi(da[i]) + r * bf16hi(ga[i]) - coef * bf16hi(xa[i]);
+      o[i] = pack_bf16x2(lo, hi);
+    }
+    *reinterpret_cast<uint4*>(dx + row * E + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+torch::Tensor rms_bwd(const torch::Tensor& dxn, const torch::Tensor& x, const torch::Tensor& rs,
+                      const c10::optional<torch::Tensor>& dres) {
+  for (const torch::Tensor* t : std::initializer_list<const torch::Tensor*>{&dxn, &x})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->sizes() == x.sizes() &&
+                    x.dim() == 2 && x.size(1) % 8 == 0,
+                "rms_bwd: contiguous bf16 [M, E] (E % 8 == 0)");
+  const __nv_bfloat16* dr = nullptr;
+  if (dres.has_value() && dres->defined()) {
+    TORCH_CHECK(dres->scalar_type() == at::kBFloat16 && dres->is_contiguous() && dres->sizes() == x.sizes(),
+                "rms_bwd: dres like x");
+    dr = reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr());
+  }
+  const at::cuda::CUDAGuard guard(x.device());
+  auto dx = torch::empty_like(x);
+  const int64_t M = x.size(0);
+  if (M == 0) return dx;
+  rms_bwd_kernel<<<(M + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dxn.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+      rs.data_ptr<float>(), dr, M, static_cast<int>(x.size(1)), reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dx;
+}
+
+// SwiGLU backward on the interleaved (gate, up) pre-activations:
+//   h = silu(g) u ;  dg = dh u silu'(g) ;  du = dh silu(g)
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh, const __nv_bfloat16* __restrict__ gu,
+                                  int64_t n_pairs, __nv_bfloat16* __restrict__ dgu) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_pairs; i += stride) {
+    const uint32_t pr = reinterpret_cast<const uint32_t*>(gu)[i];
+    const float g = bf16lo(pr), u = bf16hi(pr);
+    const float d = __bfloat162float(dh[i]);
+    const float sg = 1.0f / (1.0f + __expf(-g));
+    const float dg = d * u * sg * (1.0f + g * (1.0f - sg));
+    const float du = d * g * sg;
+    reinterpret_cast<uint32_t*>(dgu)[i] = pack_bf16x2(dg, du);
+  }
+}
+
+torch::Tensor swiglu_bwd(const torch::Tensor& dh, const torch::Tensor& gu) {
+  TORCH_CHECK(dh.is_cuda() && dh.scalar_type() == at::kBFloat16 && dh.is_contiguous(), "swiglu_bwd: bf16 dh");
+  TORCH_CHECK(gu.scalar_type() == at::kBFloat16 && gu.is_contiguous() && gu.numel() == 2 * dh.numel(),
+              "swiglu_bwd: interleaved bf16 gate/up with twice the elements of dh");
+  const at::cuda::CUDAGuard guard(dh.device());
+  auto dgu = torch::empty_like(gu);
+  const int64_t n = dh.numel();
+  if (n == 0) return dgu;
+  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 32));
+  swiglu_bwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dh.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), n,
+      reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dgu;
+}
+
 __global__ void sumsq_to_scale_kernel(const float* __restrict__ ssq, int64_t M, float inv_e, float eps,
                                       float* __restrict__ rs) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -319,7 +449,8 @@ __global__ void quant_int8_kernel(const T* __restrict__ x, int64_t R, int D, int
   float amax = 0.f;
   for (int c = lane; c < D; c += 32) amax = fmaxf(amax, fabsf(static_cast<float>(xr[c])));
   amax = warp_max(amax);
-  const float s = fmaxf(amax, 1e-12f) / 127.0f;
+  // torch evaluates `tensor / 127.0` as a multiply by the fp32 reciprocal
+  const float s = fmaxf(amax, 1e-12f) * (1.0f / 127.0f);
   for (int c = lane; c < D; c += 32) {
     float v = rintf(static_cast<float>(xr[c]) / s);
     v = fminf(fmaxf(v, -127.f), 127.f);

@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint8_t* box = staging + c * kBoxBytes;
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            v[i] *= rs;
+            v[i] *= rs * p.alpha;
             if (p.bias != nullptr) {
               const int col = n0 + c * 32 + i;
               if (col < p.N) v[i] += p.bias[col];
@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             float* o = p.out_f32 + static_cast<int64_t>(row) * p.ldo + n0 + c * 32;
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (n0 + c * 32 + i < p.N) atomicAdd(o + i, v[i]);
+              if (n0 + c * 32 + i < p.N) atomicAdd(o + i, p.alpha * v[i]);
           }
         }
       }
@@ -458,7 +458,8 @@ static const float* opt_f32(const c10::optional<torch::Tensor>& t, int64_t n, co
 
 // out = bf16((A @ W^T) * row_scale[:, None] + bias).  A [M, K]; W [N, K] (or w_kn: W stored [K, N]).
 torch::Tensor gemm_bf16(const torch::Tensor& A, const torch::Tensor& W, const c10::optional<torch::Tensor>& row_scale,
-                        const c10::optional<torch::Tensor>& bias, const torch::Tensor& status, int64_t bn, bool w_kn) {
+                        const c10::optional<torch::Tensor>& bias, const torch::Tensor& status, int64_t bn, bool w_kn,
+                        double alpha, const c10::optional<torch::Tensor>& out_opt) {
   check_operand(A, "A");
   check_operand(W, "W");
   const int64_t N = w_kn ? W.size(1) : W.size(0);
@@ -466,11 +467,14 @@ torch::Tensor gemm_bf16(const torch::Tensor& A, const torch::Tensor& W, const c1
   TORCH_CHECK(A.size(1) == K, "gemm: K mismatch");
   TORCH_CHECK(N % 8 == 0, "gemm: N must be a multiple of 8");
   const at::cuda::CUDAGuard guard(A.device());
-  auto out = torch::empty({A.size(0), N}, A.options());
+  torch::Tensor out = out_opt.has_value() && out_opt->defined() ? *out_opt : torch::empty({A.size(0), N}, A.options());
+  check_operand(out, "out");
+  TORCH_CHECK(out.size(0) == A.size(0) && out.size(1) == N, "gemm: out must be [M, N]");
   if (A.size(0) == 0) return out;
   GemmParams p = make_params(static_cast<int>(A.size(0)), static_cast<int>(N), static_cast<int>(K), status);
   p.row_scale = opt_f32(row_scale, p.M, "row_scale");
   p.bias = opt_f32(bias, p.N, "bias");
+  p.alpha = static_cast<float>(alpha);
   const int b = bn > 0 ? static_cast<int>(bn) : choose_bn(p.N);
   Operand oa{&A, false}, ow{&W, w_kn};
   auto s = at::cuda::getCurrentCUDAStream();
@@ -501,14 +505,18 @@ torch::Tensor gemm_swiglu(const torch::Tensor& A, const torch::Tensor& W, const 
 
 // out = bf16(resid + alpha * (A @ W^T)); sumsq[m] += sum_n out[m, n]^2 (if given)
 torch::Tensor gemm_residual(const torch::Tensor& A, const torch::Tensor& W, const torch::Tensor& resid, double alpha,
-                            const c10::optional<torch::Tensor>& sumsq, const torch::Tensor& status, int64_t bn) {
+                            const c10::optional<torch::Tensor>& sumsq, const torch::Tensor& status, int64_t bn,
+                            const c10::optional<torch::Tensor>& out_opt) {
   check_operand(A, "A");
   check_operand(W, "W");
   check_operand(resid, "resid");
   TORCH_CHECK(A.size(1) == W.size(1), "gemm_residual: K mismatch");
   TORCH_CHECK(resid.size(0) == A.size(0) && resid.size(1) == W.size(0), "gemm_residual: resid must be [M, N]");
   const at::cuda::CUDAGuard guard(A.device());
-  auto out = torch::empty({A.size(0), W.size(0)}, A.options());
+  torch::Tensor out =
+      out_opt.has_value() && out_opt->defined() ? *out_opt : torch::empty({A.size(0), W.size(0)}, A.options());
+  check_operand(out, "out");
+  TORCH_CHECK(out.size(0) == A.size(0) && out.size(1) == W.size(0), "gemm_residual: out must be [M, N]");
   if (A.size(0) == 0) return out;
   GemmParams p = make_params(static_cast<int>(A.size(0)), static_cast<int>(W.size(0)), static_cast<int>(A.size(1)), status);
   TORCH_CHECK(p.N % 8 == 0, "gemm_residual: N must be a multiple of 8");
@@ -523,7 +531,7 @@ torch::Tensor gemm_residual(const torch::Tensor& A, const torch::Tensor& W, cons
 // Weight gradient: out (fp32 [N_out, K_in]) += dY^T X, with dY [T, N_out], X [T, K_in]
 // (both token-major, i.e. MN-major operands), split over tokens.
 void gemm_wgrad(const torch::Tensor& dY, const torch::Tensor& X, torch::Tensor& out, const torch::Tensor& status,
-                int64_t bn, int64_t splits) {
+                int64_t bn, int64_t splits, double alpha) {
   check_operand(dY, "dY");
   check_operand(X, "X");
   TORCH_CHECK(dY.size(0) == X.size(0), "gemm_wgrad: token count mismatch");
@@ -536,6 +544,7 @@ void gemm_wgrad(const torch::Tensor& dY, const torch::Tensor& X, torch::Tensor& 
   GemmParams p = make_params(static_cast<int>(dY.size(1)), static_cast<int>(X.size(1)), T, status);
   p.out_f32 = out.data_ptr<float>();
   p.ldo = out.stride(0);
+  p.alpha = static_cast<float>(alpha);
   const int b = bn > 0 ? static_cast<int>(bn) : choose_bn(p.N);
   const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + b - 1) / b);
   const int num_kb = (T + kBK - 1) / kBK;

@@ -17,6 +17,9 @@ __all__ = [
     "attention_fwd",
     "attention_bwd",
     "rms_scale",
+    "rms_apply",
+    "rms_bwd",
+    "swiglu_bwd",
     "sumsq_to_scale",
     "pinball_loss_grad",
     "grad_sumsq",
@@ -52,12 +55,13 @@ def check_status(device: torch.device) -> None:
         raise RuntimeError(f"native kernel reported a bounded-wait timeout (status code {code})")
 
 
-def gemm(a: torch.Tensor, w: torch.Tensor, row_scale=None, bias=None, bn: int = 0, w_kn: bool = False) -> torch.Tensor:
+def gemm(a: torch.Tensor, w: torch.Tensor, row_scale=None, bias=None, bn: int = 0, w_kn: bool = False,
+         alpha: float = 1.0, out=None) -> torch.Tensor:
     """bf16 ``(a @ W.T) * row_scale[:, None] + bias`` on tcgen05 (fp32 accumulation).
 
     ``w`` is ``W`` [N, K], or with ``w_kn=True`` the same matrix stored as [K, N]
     (so ``gemm(dy, W, w_kn=True)`` is the input gradient ``dy @ W``)."""
-    return _lib().gemm_bf16(a, w, row_scale, bias, status_word(a.device), bn, w_kn)
+    return _lib().gemm_bf16(a, w, row_scale, bias, status_word(a.device), bn, w_kn, float(alpha), out)
 
 
 def gemm_swiglu(a: torch.Tensor, w_interleaved: torch.Tensor, row_scale=None, bn: int = 0) -> torch.Tensor:
@@ -65,14 +69,15 @@ def gemm_swiglu(a: torch.Tensor, w_interleaved: torch.Tensor, row_scale=None, bn
     return _lib().gemm_swiglu(a, w_interleaved, row_scale, status_word(a.device), bn)
 
 
-def gemm_residual(a, w, resid, alpha: float, sumsq=None, bn: int = 0) -> torch.Tensor:
+def gemm_residual(a, w, resid, alpha: float, sumsq=None, bn: int = 0, out=None) -> torch.Tensor:
     """bf16 ``resid + alpha * (a @ w.T)``; adds each new row's sum of squares to ``sumsq``."""
-    return _lib().gemm_residual(a, w, resid, float(alpha), sumsq, status_word(a.device), bn)
+    return _lib().gemm_residual(a, w, resid, float(alpha), sumsq, status_word(a.device), bn, out)
 
 
-def gemm_wgrad(dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor, bn: int = 0, splits: int = 0) -> torch.Tensor:
-    """``out += dy.T @ x`` in fp32 (weight gradient; split over tokens)."""
-    _lib().gemm_wgrad(dy, x, out, status_word(dy.device), bn, splits)
+def gemm_wgrad(dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor, bn: int = 0, splits: int = 0,
+               alpha: float = 1.0) -> torch.Tensor:
+    """``out += alpha * dy.T @ x`` in fp32 (weight gradient; split over tokens)."""
+    _lib().gemm_wgrad(dy, x, out, status_word(dy.device), bn, splits, float(alpha))
     return out
 
 
@@ -98,7 +103,22 @@ def attention_bwd(q, k, v, o, do, lse, dq_f32, dk, dv, *, lq, lk, lv, lo, ldo, l
 
 
 def rms_scale(x: torch.Tensor, eps: float) -> torch.Tensor:
+    """``rsqrt(mean(x**2, -1) + eps)`` per row (fp32)."""
     return _lib().rms_scale(x, float(eps))
+
+
+def rms_apply(x: torch.Tensor, rs: torch.Tensor) -> torch.Tensor:
+    return _lib().rms_apply(x, rs)
+
+
+def swiglu_bwd(dh: torch.Tensor, gu: torch.Tensor) -> torch.Tensor:
+    """Interleaved (d gate, d up) of ``h = silu(gate) * up`` given dh and interleaved (gate, up)."""
+    return _lib().swiglu_bwd(dh, gu)
+
+
+def rms_bwd(dxn: torch.Tensor, x: torch.Tensor, rs: torch.Tensor, dres=None) -> torch.Tensor:
+    """Gradient of ``x * rs(x)`` w.r.t. x, plus ``dres`` (residual-path gradient)."""
+    return _lib().rms_bwd(dxn, x, rs, dres)
 
 
 def sumsq_to_scale(ssq: torch.Tensor, E: int, eps: float) -> torch.Tensor:

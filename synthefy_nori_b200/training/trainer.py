@@ -1,0 +1,91 @@
+"""Native training step: GPU SCM-prior batch -> embedding (PyTorch) -> native encoder
+stack (sm_100a kernels, layer checkpointing) -> quantile head -> fused pinball
+objective -> backward -> data-parallel gradient reduction -> fused AdamW + EMA.
+
+Reference step: ``training/trainer.py:1230-1578`` (bf16 autocast forward, pinball
+loss, backward, clip 1.0, optimizer, EMA).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from synthefy_nori_b200.training.loss import pinball_objective
+from synthefy_nori_b200.training.optim import FlatParams, FusedAdamWEMA
+
+
+@dataclass
+class TrainConfig:
+    lr: float = 3e-4
+    weight_decay: float = 0.01
+    betas: tuple = (0.9, 0.95)
+    eps: float = 1e-8
+    ema_decay: float | None = 0.999
+    max_grad_norm: float = 1.0
+    pinball_tail_weight: float = 0.0
+    pinball_monotonicity_weight: float = 0.05
+    pinball_mse_weight: float = 0.0
+    checkpoint_layers: bool = True
+    grad_reduction: str = "nccl"  # "nccl" | "peer" (in-kernel reduce-scatter over NVLink peer memory)
+    extra: dict = field(default_factory=dict)
+
+
+def forward_native(model, x: torch.Tensor, y_ctx: torch.Tensor, eval_pos: int, checkpoint_layers: bool = True):
+    """Regression head output [B, Nq, K] of ``model`` on the native encoder stack."""
+    from synthefy_nori_b200.ops.fused_layer import Geometry, check_supported, run_stack_tokens, tokens_to_rows
+
+    check_supported(model)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        xe, ye, _pre, _pad, _my = model.embed(x, y_ctx, eval_pos, "reg")
+        tokens = torch.cat((xe, ye.unsqueeze(2).to(xe.dtype)), 2)
+    B, S, T, E = tokens.shape
+    g = Geometry(B=B, ep=eval_pos, nq=S - eval_pos, T=T, E=E, H=model.nhead)
+    X = tokens_to_rows(tokens, eval_pos)
+    X = run_stack_tokens(model, X, g, checkpoint_layers)
+    tgt = X[g.R_ctx :].view(B, S - eval_pos, T, E)[:, :, -1]
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = model.encoder_out_norm(tgt)
+        return model.reg_y_decoder(out)
+
+
+class NoriTrainer:
+    def __init__(self, model, cfg: TrainConfig, device: torch.device, process_group=None):
+        self.model = model.to(device)
+        self.model.train()
+        self.cfg = cfg
+        self.device = device
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group) if (dist.is_available() and dist.is_initialized()) else 1
+        if self.world > 1:
+            for p in self.model.parameters():  # identical initial weights on every rank
+                dist.broadcast(p.data, 0, group=process_group)
+        self.flat = FlatParams(self.model.parameters(), device)
+        self.opt = FusedAdamWEMA(self.flat, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps, weight_decay=cfg.weight_decay,
+                                 ema_decay=cfg.ema_decay, max_grad_norm=cfg.max_grad_norm)
+        self.quantiles = torch.tensor(model.regression_quantiles, device=device, dtype=torch.float32)
+        self.reducer = None
+        if self.world > 1 and cfg.grad_reduction == "peer":
+            from synthefy_nori_b200.parallel.peer_reduce import PeerGradReducer
+
+            self.reducer = PeerGradReducer(self.flat.grad, process_group)
+
+    def train_step(self, x: torch.Tensor, y: torch.Tensor, eval_pos: int) -> torch.Tensor:
+        """One optimizer step on tables ``x [B, N, F]`` with targets ``y [B, N]``.
+        Returns the (device) loss."""
+        self.flat.zero_grad()
+        pred = forward_native(self.model, x, y[:, :eval_pos], eval_pos, self.cfg.checkpoint_layers)
+        loss = pinball_objective(pred, y[:, eval_pos:], self.quantiles, self.cfg.pinball_tail_weight,
+                                 self.cfg.pinball_monotonicity_weight, self.cfg.pinball_mse_weight)
+        loss.backward()
+        scale = 1.0
+        if self.world > 1:
+            if self.reducer is not None:
+                self.reducer.all_reduce_sum()
+            else:
+                dist.all_reduce(self.flat.grad, group=self.pg)
+            scale = 1.0 / self.world
+        self.opt.step(grad_scale=scale)
+        return loss.detach()

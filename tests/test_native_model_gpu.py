@@ -1,0 +1,82 @@
+"""The native encoder stack (tcgen05 GEMMs, flash attention, fused RMSNorm / SwiGLU /
+residual epilogues, explicit backward) against the fp32 PyTorch model."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from synthefy_nori_b200.models.config import preset_config  # noqa: E402
+from synthefy_nori_b200.training.loss import pinball_objective, pinball_objective_torch  # noqa: E402
+from synthefy_nori_b200.training.trainer import forward_native  # noqa: E402
+from synthefy_nori_b200.utils.loading import build_model  # noqa: E402
+
+
+def _model(name, seed=0):
+    torch.manual_seed(seed)
+    m = build_model(preset_config(name)).cuda()
+    g = torch.Generator().manual_seed(1)
+    with torch.no_grad():
+        for _, p in m.named_parameters():
+            if p.abs().sum() == 0:
+                p.copy_((torch.randn(p.shape, generator=g) * 0.05).to(p))
+    return m
+
+
+def _data(B=2, S=120, F=9, ep=80, seed=3):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, S, F, generator=g)
+    x[torch.rand(B, S, F, generator=g) < 0.05] = float("nan")
+    y = torch.randn(B, S, generator=g)
+    return x.cuda(), y.cuda(), ep
+
+
+def _cos(a, b):
+    a, b = a.flatten().double(), b.flatten().double()
+    return float((a @ b) / (a.norm() * b.norm() + 1e-30))
+
+
+@pytest.mark.parametrize("name", ["nori-tiny", "nori-6m"])
+def test_native_forward_matches_fp32(name):
+    m = _model(name).eval()
+    x, y, ep = _data()
+    with torch.no_grad():
+        ref = m(x, y[:, :ep], ep, task_type="reg").float()
+        out = forward_native(m, x, y[:, :ep], ep, checkpoint_layers=False).float()
+    err = (out - ref).abs().max().item()
+    assert _cos(out, ref) > 0.999, err
+    assert err < 0.05 * ref.abs().max().item() + 0.05
+
+
+def test_native_backward_matches_fp32():
+    m = _model("nori-tiny").train()
+    x, y, ep = _data()
+    q = torch.tensor(m.regression_quantiles, device="cuda")
+    m.zero_grad()
+    ref = pinball_objective_torch(m(x, y[:, :ep], ep, task_type="reg"), y[:, ep:], q, 0.0, 0.05, 0.1)
+    ref.backward()
+    ref_grads = {n: p.grad.clone() for n, p in m.named_parameters() if p.grad is not None}
+    m.zero_grad()
+    loss = pinball_objective(forward_native(m, x, y[:, :ep], ep, checkpoint_layers=True), y[:, ep:], q, 0.0, 0.05, 0.1)
+    loss.backward()
+    assert abs(loss.item() - ref.item()) < 0.02 * abs(ref.item()) + 1e-3
+    bad = []
+    for n, p in m.named_parameters():
+        if n not in ref_grads or ref_grads[n].abs().max() < 1e-8:
+            continue
+        c = _cos(p.grad, ref_grads[n])
+        if c < 0.98:
+            bad.append((n, c))
+    assert not bad, bad
+
+
+def test_trainer_reduces_loss_on_fixed_batch():
+    from synthefy_nori_b200.training.prior import PriorConfig, scm_prior_batch
+    from synthefy_nori_b200.training.trainer import NoriTrainer, TrainConfig
+
+    m = _model("nori-tiny")
+    tr = NoriTrainer(m, TrainConfig(lr=1e-3, ema_decay=0.99), torch.device("cuda"))
+    b = scm_prior_batch(PriorConfig(max_features=10, pad_features=10), 4, 128, 96, seed=5, device=torch.device("cuda"))
+    losses = [tr.train_step(b.x, b.y, b.eval_pos).item() for _ in range(12)]
+    assert all(torch.isfinite(torch.tensor(losses)))
+    assert losses[-1] < losses[0]
