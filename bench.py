@@ -4,7 +4,8 @@
 
 For N > 1 run under ``torch.distributed.run`` (one rank per GPU, NCCL, rendezvous on
 127.0.0.1).  Config (nori-100m training on the config-3 table shapes):
-random-init nori-100m weights, synthetic SCM-prior tables, 32 tables per GPU per step,
+random-init nori-100m weights, synthetic SCM-prior tables, 16 tables per GPU per step
+(32, the nori-30m config's batch, does not fit the reference's nori-100m step in 180 GB),
 rows ~ U[512, 2048] (one row count per step, shared by the batch), context fraction
 ~ U[0.5, 0.9], features ~ U[5, 100] padded to 100, 999-quantile pinball loss (+0.05
 monotonicity), bf16 compute, clip 1.0, AdamW + EMA 0.999, activation checkpointing.
@@ -35,8 +36,10 @@ import sys
 import tempfile
 import time
 
-import torch
-import torch.distributed as dist
+os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
@@ -52,7 +55,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--model", default="nori-100m")
-    ap.add_argument("--tables-per-gpu", type=int, default=32)
+    ap.add_argument("--tables-per-gpu", type=int, default=16)
     ap.add_argument("--min-rows", type=int, default=512)
     ap.add_argument("--max-rows", type=int, default=2048)
     ap.add_argument("--features", type=int, default=100)

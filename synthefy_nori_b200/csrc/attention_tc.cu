@@ -1,0 +1,387 @@
+// Flash attention forward on the 5th-generation tensor cores (tcgen05 + TMEM + TMA),
+// used for the long sequence (ICL) attention of the Nori encoder: context
+// self-attention and query->context cross-attention per (table, column, head)
+// (reference model/layer.py:1407-1441, 685-745).
+//
+// One CTA = 128 query rows of one head. Warp roles (256 threads):
+//   warp 0      TMA producer: the Q tile once, then 128-key K / V tiles into a
+//               2-stage ring (5-D tensor maps read the strided token-major layouts
+//               directly; head-dim padding and tails are zero-filled by TMA);
+//   warp 1      TMEM owner + MMA issuer: S_j = Q K_j^T (M=128, N=128, K=64) into one
+//               of two TMEM score buffers, then O_j = P_j V_j (M=128, N=64, K=128,
+//               V read MN-major) into one of two TMEM output buffers;
+//   warps 4..7  softmax: one thread per query row (its TMEM lane); reads S_j, keeps
+//               the running max / sum, writes P_j (bf16) to shared memory in the
+//               128B-swizzled K-major layout the MMA reads, and accumulates
+//               O += alpha * O_j in registers.
+// Score tile j+1 is computed by the tensor core while the softmax of tile j runs.
+//
+// Every mbarrier wait is bounded (see sm100.cuh); on timeout the CTA records an error
+// in the status word and returns after freeing its TMEM.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <algorithm>
+#include <array>
+
+#include "sm100.cuh"
+#include "tma_host.h"
+
+namespace nori {
+
+namespace fa {
+constexpr int kM = 128;      // query rows per CTA
+constexpr int kN = 128;      // keys per tile
+constexpr int kD = 64;       // padded head dim
+constexpr int kThreads = 256;
+constexpr int kTileBytes = kM * kD * 2;  // 16 KB (Q, K or V tile)
+constexpr int kPBytes = kM * kN * 2;     // 32 KB (P tile: two 64-key panels)
+// smem: Q | K[2] | V[2] | P[2] | barriers
+constexpr int kSmemBytes = kTileBytes * 5 + kPBytes * 2 + 1024 + 256;
+constexpr uint32_t kTmemCols = 512;  // S[2] (2 x 128) + O[2] (2 x 64) -> 384 used
+}  // namespace fa
+
+struct AttnTcParams {
+  int Nq, Nk, d_valid;
+  float scale_log2;
+  // coordinate positions (inside the 5-D maps) of row / i2 / i1 / i0 for Q and for K/V
+  int q_pos[4], kv_pos[4];
+  int d1, d2;  // bh decomposition
+  __nv_bfloat16* o;
+  int64_t o_s0, o_s1, o_s2, o_row;
+  float* lse;
+  int* status;
+};
+
+__device__ __forceinline__ void coords_for(const int (&pos)[4], int row, int i2, int i1, int i0, int (&c)[5]) {
+  c[0] = 0;
+  c[pos[0]] = row;
+  c[pos[1]] = i2;
+  c[pos[2]] = i1;
+  c[pos[3]] = i0;
+}
+
+__global__ void __launch_bounds__(fa::kThreads, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, AttnTcParams p) {
+  using namespace fa;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kTileBytes;            // 2 stages
+  uint8_t* sV = sK + 2 * kTileBytes;        // 2 stages
+  uint8_t* sP = sV + 2 * kTileBytes;        // 2 buffers of 32 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* p_full = bars + 7;    // [2]
+  uint64_t* o_full = bars + 9;    // [2]
+  uint64_t* o_free = bars + 11;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t bh = blockIdx.y;
+  const int q0 = blockIdx.x * kM;
+  const int i2 = static_cast<int>(bh % p.d2);
+  const int i1 = static_cast<int>((bh / p.d2) % p.d1);
+  const int i0 = static_cast<int>(bh / (static_cast<int64_t>(p.d1) * p.d2));
+  const int n_tiles = (p.Nk + kN - 1) / kN;
+  // a CTA that starts after another one timed out returns at once
+  if (p.status != nullptr && *reinterpret_cast<volatile int*>(p.status) != 0) return;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem;            // S buffers at columns 0, 128
+  const uint32_t tO = tmem + 2 * kN;   // O buffers at columns 256, 320
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      int c[5];
+      coords_for(p.q_pos, q0, i2, i1, i0, c);
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_5d(sQ, &tmQ, q_full, c);
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, p.status, kTimeoutProducer, abort_flag)) break;
+        coords_for(p.kv_pos, j * kN, i2, i1, i0, c);
+        mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
+        tma_load_5d(sK + s * kTileBytes, &tmK, &kv_full[s], c);
+        tma_load_5d(sV + s * kTileBytes, &tmV, &kv_full[s], c);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(kM, kN, false, false);
+      constexpr uint32_t idesc_o = umma_idesc_bf16(kM, kD, false, true);
+      const uint32_t aQ = smem_u32(sQ);
+      bool ok = mbar_wait(q_full, 0, p.status, kTimeoutMma, abort_flag);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, p.status, kTimeoutMma, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t bK = smem_u32(sK + s * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k)
+          umma_bf16_ss(tS + s * kN, umma_desc_kmajor_sw128(aQ + k * 32), umma_desc_kmajor_sw128(bK + k * 32), idesc_s,
+                       k > 0 ? 1u : 0u);
+        umma_commit(&s_full[s]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int s = j & 1;
+        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+        if (!mbar_wait(&p_full[s], (j >> 1) & 1, p.status, kTimeoutMma, abort_flag)) break;
+        if (j >= 2 && !mbar_wait(&o_free[s], ((j >> 1) & 1) ^ 1, p.status, kTimeoutMma, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t aP = smem_u32(sP + s * kPBytes);
+        const uint32_t bV = smem_u32(sV + s * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < kN / 16; ++k) {
+          const uint64_t da = umma_desc_kmajor_sw128(aP + (k >> 2) * (kM * 128) + (k & 3) * 32);
+          const uint64_t db = umma_smem_desc(bV + k * 2048, 8192, 1024, 2);
+          umma_bf16_ss(tO + s * kD, da, db, idesc_o, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&o_full[s]);
+        umma_commit(&kv_empty[s]);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // row in tile == TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    float m_prev = -INFINITY, m_cur = -INFINITY, l = 0.f;
+    float o[kD];
+#pragma unroll
+    for (int i = 0; i < kD; ++i) o[i] = 0.f;
+    bool ok = true;
+    auto absorb = [&](int j, float a) -> bool {
+      const int s = j & 1;
+      if (!mbar_wait(&o_full[s], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) return false;
+      tc_fence_after();
+      uint32_t v[32];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        tmem_ld32(tO + s * kD + lane_off + h * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[h * 32 + i] = o[h * 32 + i] * a + __uint_as_float(v[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(&o_free[s]);
+      return true;
+    };
+    float alpha_pending = 1.f;
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait(&s_full[s], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int valid = min(kN, p.Nk - j * kN);
+      const uint32_t ts = tS + s * kN + lane_off;
+      // pass 1: row max
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(ts + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(v[i]));
+      }
+      const float m_new = fmaxf(m_cur, mx * p.scale_log2);
+      const float a = exp2f(m_cur - m_new);  // m_cur = -inf on the first tile -> 0
+      // pass 2: P = exp2(s * scale - m), row sum, bf16 P into swizzled smem
+      float rsum = 0.f;
+      uint8_t* prow = sP + s * kPBytes;
+#pragma unroll
+      for (int c = 0; c < kN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(ts + c * 32, v);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int col = c * 32 + 2 * i;
+          const float e0 = col < valid ? exp2f(__uint_as_float(v[2 * i]) * p.scale_log2 - m_new) : 0.f;
+          const float e1 = col + 1 < valid ? exp2f(__uint_as_float(v[2 * i + 1]) * p.scale_log2 - m_new) : 0.f;
+          pk[i] = pack_bf16x2(e0, e1);
+          rsum += bf16lo(pk[i]) + bf16hi(pk[i]);
+        }
+        // 32 keys = 4 chunks of 16 bytes in panel (c >> 1), chunks (c & 1) * 4 ..
+        uint8_t* panel = prow + (c >> 1) * (kM * 128);
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int chunk = (c & 1) * 4 + cc;
+          *reinterpret_cast<uint4*>(panel + r * 128 + ((chunk ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+        }
+      }
+      l = l * a + rsum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[s]);
+      // absorb the previous tile's P V (scaled to the max of that tile)
+      if (j >= 1) {
+        if (!absorb(j - 1, alpha_pending)) {
+          ok = false;
+          break;
+        }
+      }
+      alpha_pending = a;  // O (relative to m_{j-1}) -> relative to m_j when tile j is absorbed
+      m_prev = m_cur;
+      m_cur = m_new;
+    }
+    if (ok && n_tiles > 0) ok = absorb(n_tiles - 1, alpha_pending);
+    (void)m_prev;
+    if (ok) {
+      const int row = q0 + r;
+      if (row < p.Nq) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        __nv_bfloat16* out = p.o + static_cast<int64_t>(i0) * p.o_s0 + static_cast<int64_t>(i1) * p.o_s1 +
+                             static_cast<int64_t>(i2) * p.o_s2 + static_cast<int64_t>(row) * p.o_row;
+#pragma unroll
+        for (int c8 = 0; c8 < kD / 8; ++c8) {
+          if (c8 * 8 < p.d_valid) {
+            *reinterpret_cast<uint4*>(out + c8 * 8) =
+                make_uint4(pack_bf16x2(o[c8 * 8] * inv, o[c8 * 8 + 1] * inv),
+                           pack_bf16x2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv),
+                           pack_bf16x2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv),
+                           pack_bf16x2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv));
+          }
+        }
+        if (p.lse != nullptr) {
+          constexpr float kLn2 = 0.6931471805599453f;
+          p.lse[bh * p.Nq + row] = l > 0.f ? (m_cur + log2f(l)) * kLn2 : -INFINITY;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host
+namespace {
+
+struct Map5 {
+  CUtensorMap map;
+  int pos[4];  // positions of row, i2, i1, i0
+};
+
+// Layout (s0, s1, s2, row, d1, d2) of a [.., rows, d] view -> 5-D map with the non-contiguous
+// dimensions sorted by stride (the box is 64 x 1 x .. x 128 rows x ..).
+Map5 make_map(const torch::Tensor& t, const std::vector<int64_t>& l, int64_t n_rows, int64_t n_i0, int d_valid) {
+  struct Dim {
+    int64_t extent, stride;
+    int role;  // 0 row, 1 i2, 2 i1, 3 i0
+  };
+  const int64_t d1 = l[4], d2 = l[5];
+  std::array<Dim, 4> dims = {Dim{n_rows, l[3], 0}, Dim{d2, l[2], 1}, Dim{d1, l[1], 2}, Dim{n_i0, l[0], 3}};
+  // dimensions of extent 1 get a harmless stride (never stepped)
+  int64_t big = 1;
+  for (auto& d : dims) big = std::max(big, d.stride * std::max<int64_t>(d.extent, 1));
+  for (auto& d : dims)
+    if (d.extent <= 1 || d.stride == 0) d.stride = big;
+  std::stable_sort(dims.begin(), dims.end(), [](const Dim& a, const Dim& b) { return a.stride < b.stride; });
+  int64_t ext[5], strides[4];
+  int box[5];
+  ext[0] = d_valid;
+  box[0] = fa::kD;
+  Map5 m{};
+  for (int i = 0; i < 4; ++i) {
+    ext[i + 1] = std::max<int64_t>(dims[i].extent, 1);
+    strides[i] = dims[i].stride * 2;
+    box[i + 1] = dims[i].role == 0 ? fa::kM : 1;
+    m.pos[dims[i].role] = i + 1;
+  }
+  m.map = make_tmap_nd_bf16(t.data_ptr(), 5, ext, strides, box);
+  return m;
+}
+
+}  // namespace
+
+void attn_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
+                 const c10::optional<torch::Tensor>& lse, std::vector<int64_t> lq, std::vector<int64_t> lk,
+                 std::vector<int64_t> lv, std::vector<int64_t> lo, int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid,
+                 double scale, const torch::Tensor& status) {
+  for (const torch::Tensor* t : std::initializer_list<const torch::Tensor*>{&q, &k, &v, &o})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16, "attn_fwd_tc: bf16 CUDA tensors");
+  TORCH_CHECK(d_valid > 0 && d_valid <= fa::kD && d_valid % 8 == 0, "attn_fwd_tc: head dim multiple of 8, <= 64");
+  TORCH_CHECK(lk == lv || (lk[4] == lv[4] && lk[5] == lv[5]), "attn_fwd_tc: K and V share the head decomposition");
+  TORCH_CHECK(lq[4] == lk[4] && lq[5] == lk[5] && lq[4] == lo[4] && lq[5] == lo[5],
+              "attn_fwd_tc: Q / K / V / O share the head decomposition");
+  for (int i = 0; i < 4; ++i) TORCH_CHECK(lo[i] % 8 == 0, "attn_fwd_tc: output rows must be 16-byte aligned");
+  const at::cuda::CUDAGuard guard(q.device());
+  if (BH == 0 || Nq == 0) return;
+  TORCH_CHECK(Nk > 0, "attn_fwd_tc: at least one key");
+  const int64_t n_i0 = BH / (lq[4] * lq[5]);
+  TORCH_CHECK(n_i0 * lq[4] * lq[5] == BH, "attn_fwd_tc: BH must equal i0 * d1 * d2");
+  Map5 mq = make_map(q, lq, Nq, n_i0, static_cast<int>(d_valid));
+  Map5 mk = make_map(k, lk, Nk, n_i0, static_cast<int>(d_valid));
+  Map5 mv = make_map(v, lv, Nk, n_i0, static_cast<int>(d_valid));
+  TORCH_CHECK(std::equal(mk.pos, mk.pos + 4, mv.pos), "attn_fwd_tc: K and V layouts must sort alike");
+  AttnTcParams p{};
+  p.Nq = static_cast<int>(Nq);
+  p.Nk = static_cast<int>(Nk);
+  p.d_valid = static_cast<int>(d_valid);
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  std::copy(mq.pos, mq.pos + 4, p.q_pos);
+  std::copy(mk.pos, mk.pos + 4, p.kv_pos);
+  p.d1 = static_cast<int>(lq[4]);
+  p.d2 = static_cast<int>(lq[5]);
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.o_s0 = lo[0];
+  p.o_s1 = lo[1];
+  p.o_s2 = lo[2];
+  p.o_row = lo[3];
+  if (lse.has_value() && lse->defined()) {
+    TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->numel() >= BH * Nq, "attn_fwd_tc: fp32 lse [BH, Nq]");
+    p.lse = lse->data_ptr<float>();
+  }
+  p.status = status.defined() && status.numel() > 0 ? status.data_ptr<int>() : nullptr;
+  static bool configured[64] = {false};
+  const int dev = q.get_device();
+  if (!configured[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::kSmemBytes));
+    configured[dev] = true;
+  }
+  TORCH_CHECK(BH <= 65535LL * 65535LL, "attn_fwd_tc: too many heads");
+  dim3 grid(static_cast<unsigned>((Nq + fa::kM - 1) / fa::kM), static_cast<unsigned>(BH));
+  attn_fwd_tc_kernel<<<grid, fa::kThreads, fa::kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(mq.map, mk.map, mv.map, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace nori

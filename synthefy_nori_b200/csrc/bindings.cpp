@@ -25,6 +25,10 @@ void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
               torch::Tensor& dv, std::vector<int64_t> lq, std::vector<int64_t> lk, std::vector<int64_t> lv,
               std::vector<int64_t> lo, std::vector<int64_t> ldo, std::vector<int64_t> ldk, std::vector<int64_t> ldv,
               int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid, double scale);
+void attn_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
+                 const c10::optional<torch::Tensor>& lse, std::vector<int64_t> lq, std::vector<int64_t> lk,
+                 std::vector<int64_t> lv, std::vector<int64_t> lo, int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid,
+                 double scale, const torch::Tensor& status);
 torch::Tensor rms_scale(const torch::Tensor& x, double eps);
 torch::Tensor sumsq_to_scale(const torch::Tensor& ssq, int64_t E, double eps);
 std::vector<torch::Tensor> pinball_fused(const torch::Tensor& pred, const torch::Tensor& target,
@@ -46,6 +50,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_wgrad", &nori::gemm_wgrad);
   m.def("attn_fwd", &nori::attn_fwd);
   m.def("attn_bwd", &nori::attn_bwd);
+  m.def("attn_fwd_tc", &nori::attn_fwd_tc);
   m.def("rms_scale", &nori::rms_scale);
   m.def("rms_apply", &nori::rms_apply);
   m.def("swiglu_bwd", &nori::swiglu_bwd);

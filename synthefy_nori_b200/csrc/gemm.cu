@@ -102,6 +102,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int num_n = (p.N + BN - 1) / BN;
   const int num_kb = (p.K + kBK - 1) / kBK;
   const int items = num_m * num_n * p.k_splits;
+  // a CTA that starts after another one timed out returns at once
+  if (p.status != nullptr && *reinterpret_cast<volatile int*>(p.status) != 0) return;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {

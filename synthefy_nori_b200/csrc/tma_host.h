@@ -47,3 +47,32 @@ inline CUtensorMap make_tmap_2d_bf16(void* base, int64_t cols, int64_t rows, int
 }
 
 }  // namespace nori
+
+namespace nori {
+
+// Up-to-5-D bf16 tensor map: dims[0] is the contiguous dimension; strides_bytes[i] is
+// the byte stride of dims[i + 1]; box[i] elements per dimension; 128B swizzle.
+inline CUtensorMap make_tmap_nd_bf16(void* base, int rank, const int64_t* dims, const int64_t* strides_bytes,
+                                     const int* box, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK(rank >= 1 && rank <= 5, "TMA rank 1..5");
+  CUtensorMap m;
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = static_cast<cuuint64_t>(dims[i]);
+    b[i] = static_cast<cuuint32_t>(box[i]);
+    e[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) {
+    TORCH_CHECK(strides_bytes[i] % 16 == 0, "TMA strides must be multiples of 16 bytes");
+    s[i] = static_cast<cuuint64_t>(strides_bytes[i]);
+  }
+  CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, base, d, s, b, e,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (rank ", rank, ") failed with code ", static_cast<int>(r));
+  return m;
+}
+
+}  // namespace nori

@@ -16,6 +16,7 @@ __all__ = [
     "gemm_wgrad",
     "attention_fwd",
     "attention_bwd",
+    "attention_fwd_tc",
     "rms_scale",
     "rms_apply",
     "rms_bwd",
@@ -92,6 +93,14 @@ def attention_fwd(q, k, v, o, *, lq, lk, lv, lo, BH, Nq, Nk, d, scale, lse=None)
     ``bh`` starts at element ``i0*s0 + i1*s1 + i2*s2 + r*row_stride`` of the tensor."""
     _lib().attn_fwd(q, k, v, o, lse, _layout(lq), _layout(lk), _layout(lv), _layout(lo), int(BH), int(Nq), int(Nk),
                     int(d), float(scale))
+    return o
+
+
+def attention_fwd_tc(q, k, v, o, *, lq, lk, lv, lo, BH, Nq, Nk, d, scale, lse=None):
+    """tcgen05 / TMEM flash attention forward (128-row query tiles, 128-key tiles);
+    same layout convention as ``attention_fwd``."""
+    _lib().attn_fwd_tc(q, k, v, o, lse, _layout(lq), _layout(lk), _layout(lv), _layout(lo), int(BH), int(Nq), int(Nk),
+                       int(d), float(scale), status_word(q.device))
     return o
 
 

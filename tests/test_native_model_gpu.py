@@ -40,12 +40,17 @@ def _cos(a, b):
 def test_native_forward_matches_fp32(name):
     m = _model(name).eval()
     x, y, ep = _data()
+    m.impl = "torch"
     with torch.no_grad():
         ref = m(x, y[:, :ep], ep, task_type="reg").float()
         out = forward_native(m, x, y[:, :ep], ep, checkpoint_layers=False).float()
     err = (out - ref).abs().max().item()
     assert _cos(out, ref) > 0.999, err
     assert err < 0.05 * ref.abs().max().item() + 0.05
+    m.impl = "auto"  # model.forward on CUDA runs the native stack
+    with torch.no_grad():
+        auto = m(x, y[:, :ep], ep, task_type="reg").float()
+    assert _cos(auto, ref) > 0.999
 
 
 def test_native_backward_matches_fp32():
@@ -53,6 +58,7 @@ def test_native_backward_matches_fp32():
     x, y, ep = _data()
     q = torch.tensor(m.regression_quantiles, device="cuda")
     m.zero_grad()
+    m.impl = "torch"
     ref = pinball_objective_torch(m(x, y[:, :ep], ep, task_type="reg"), y[:, ep:], q, 0.0, 0.05, 0.1)
     ref.backward()
     ref_grads = {n: p.grad.clone() for n, p in m.named_parameters() if p.grad is not None}
