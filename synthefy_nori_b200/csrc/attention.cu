@@ -101,17 +101,150 @@ struct AttnFwdParams {
   float* lse;  // [BH, Nq] or null
   Layout3 lq, lk, lv, lo;
   int BH, Nq, Nk, d_valid;  // d_valid: true head dim (<= 64) of the output
+  int n_tiles_q;
   int q_d_valid;            // columns of Q / K / V to read (<= 64)
   float scale_log2;         // softmax scale * log2(e)
 };
+
+// Per-warp running state of the forward pass (16 query rows per warp).
+struct FwdState {
+  uint32_t qf[4][4];
+  float o[8][4];
+  float m0, m1, l0, l1;
+};
+
+__device__ __forceinline__ void fwd_init(FwdState& st, const uint8_t* sq, int warp, int lane) {
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const int r = warp * 16 + (lane & 15);
+    const int c = kk * 2 + (lane >> 4);
+    ldsm_x4(st.qf[kk], smem_u32(sq + swz(r, c)));
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) st.o[i][0] = st.o[i][1] = st.o[i][2] = st.o[i][3] = 0.f;
+  st.m0 = st.m1 = -INFINITY;
+  st.l0 = st.l1 = 0.f;
+}
+
+// One 64-key tile: S = Q K^T, online softmax, O += P V.
+__device__ __forceinline__ void fwd_tile(FwdState& st, const uint8_t* sk, const uint8_t* sv, int kbase, int Nk,
+                                         float scale_log2, int lane) {
+  float s[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+    for (int j2 = 0; j2 < 4; ++j2) {
+      // two key n-tiles (16 keys) x 16 d: (keys 0-7, d lo), (keys 0-7, d hi), (keys 8-15, d lo), (8-15, d hi)
+      uint32_t b[4];
+      const int key = j2 * 16 + (lane & 7) + ((lane >> 4) << 3);
+      const int c = kk * 2 + ((lane >> 3) & 1);
+      ldsm_x4(b, smem_u32(sk + swz(key, c)));
+      mma16816(s[2 * j2], st.qf[kk], b[0], b[1]);
+      mma16816(s[2 * j2 + 1], st.qf[kk], b[2], b[3]);
+    }
+  }
+  if (kbase + kBlkK > Nk) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c0 = kbase + j * 8 + (lane & 3) * 2;
+      if (c0 >= Nk) s[j][0] = s[j][2] = -INFINITY;
+      if (c0 + 1 >= Nk) s[j][1] = s[j][3] = -INFINITY;
+    }
+  }
+  float mx0 = st.m0, mx1 = st.m1;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]) * scale_log2);
+    mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]) * scale_log2);
+  }
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+  }
+  const float a0 = (st.m0 == -INFINITY) ? 0.f : exp2f(st.m0 - mx0);
+  const float a1 = (st.m1 == -INFINITY) ? 0.f : exp2f(st.m1 - mx1);
+  const float mb0 = (mx0 == -INFINITY) ? 0.f : mx0;
+  const float mb1 = (mx1 == -INFINITY) ? 0.f : mx1;
+  st.m0 = mx0;
+  st.m1 = mx1;
+  float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    s[j][0] = exp2f(s[j][0] * scale_log2 - mb0);
+    s[j][1] = exp2f(s[j][1] * scale_log2 - mb0);
+    s[j][2] = exp2f(s[j][2] * scale_log2 - mb1);
+    s[j][3] = exp2f(s[j][3] * scale_log2 - mb1);
+    rs0 += s[j][0] + s[j][1];
+    rs1 += s[j][2] + s[j][3];
+  }
+  st.l0 = st.l0 * a0 + rs0;
+  st.l1 = st.l1 * a1 + rs1;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    st.o[i][0] *= a0;
+    st.o[i][1] *= a0;
+    st.o[i][2] *= a1;
+    st.o[i][3] *= a1;
+  }
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    uint32_t pa[4];
+    pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+    pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+    pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+    pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+    for (int i2 = 0; i2 < 4; ++i2) {
+      uint32_t b[4];
+      const int key = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+      const int c = i2 * 2 + (lane >> 4);
+      ldsm_x4_t(b, smem_u32(sv + swz(key, c)));
+      mma16816(st.o[2 * i2], pa, b[0], b[1]);
+      mma16816(st.o[2 * i2 + 1], pa, b[2], b[3]);
+    }
+  }
+}
+
+__device__ __forceinline__ void fwd_store(FwdState& st, __nv_bfloat16* ob, int64_t row_stride, float* lse, int64_t bh,
+                                          int q0, int Nq, int d_valid, int warp, int lane) {
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    st.l0 += __shfl_xor_sync(0xffffffffu, st.l0, off);
+    st.l1 += __shfl_xor_sync(0xffffffffu, st.l1, off);
+  }
+  const float inv0 = st.l0 > 0.f ? 1.f / st.l0 : 0.f;
+  const float inv1 = st.l1 > 0.f ? 1.f / st.l1 : 0.f;
+  const int r0 = q0 + warp * 16 + (lane >> 2);
+  const int r1 = r0 + 8;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c = i * 8 + (lane & 3) * 2;
+    if (c < d_valid) {
+      if (r0 < Nq)
+        *reinterpret_cast<uint32_t*>(ob + static_cast<int64_t>(r0) * row_stride + c) =
+            pack_bf16x2(st.o[i][0] * inv0, st.o[i][1] * inv0);
+      if (r1 < Nq)
+        *reinterpret_cast<uint32_t*>(ob + static_cast<int64_t>(r1) * row_stride + c) =
+            pack_bf16x2(st.o[i][2] * inv1, st.o[i][3] * inv1);
+    }
+  }
+  if (lse != nullptr && (lane & 3) == 0) {
+    constexpr float kLn2 = 0.6931471805599453f;
+    if (r0 < Nq) lse[bh * Nq + r0] = st.l0 > 0.f ? (st.m0 + log2f(st.l0)) * kLn2 : -INFINITY;
+    if (r1 < Nq) lse[bh * Nq + r1] = st.l1 > 0.f ? (st.m1 + log2f(st.l1)) * kLn2 : -INFINITY;
+  }
+}
 
 __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwdParams p) {
   __shared__ __align__(128) uint8_t sq[kBlkQ * 128];
   __shared__ __align__(128) uint8_t sk[2][kBlkK * 128];
   __shared__ __align__(128) uint8_t sv[2][kBlkK * 128];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t bh = blockIdx.y;
-  const int q0 = blockIdx.x * kBlkQ;
+  const int64_t bh = blockIdx.x / p.n_tiles_q;
+  const int q0 = static_cast<int>(blockIdx.x % p.n_tiles_q) * kBlkQ;
   const __nv_bfloat16* qb = p.q + p.lq.offset(bh, 0);
   const __nv_bfloat16* kb = p.k + p.lk.offset(bh, 0);
   const __nv_bfloat16* vb = p.v + p.lv.offset(bh, 0);
@@ -122,12 +255,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwdParams p)
   cp_async_commit();
 
   const int n_tiles = (p.Nk + kBlkK - 1) / kBlkK;
-  uint32_t qf[4][4];
-  float o[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
+  FwdState st;
   for (int t = 0; t < n_tiles; ++t) {
     const int buf = t & 1;
     if (t + 1 < n_tiles) {
@@ -137,128 +265,79 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwdParams p)
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    if (t == 0) {
-      // Q fragments: rows warp*16 .. +15, k chunks of 16 columns
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const int r = warp * 16 + (lane & 15);
-        const int c = kk * 2 + (lane >> 4);
-        ldsm_x4(qf[kk], smem_u32(sq + swz(r, c)));
-      }
-    }
-    // S = Q K^T : 16 x 64 per warp
-    float s[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int j2 = 0; j2 < 4; ++j2) {
-        // two key n-tiles (16 keys) x 16 d: matrices (keys 0-7, d lo), (keys 0-7, d hi), (keys 8-15, d lo), (8-15, d hi)
-        uint32_t b[4];
-        const int key = j2 * 16 + (lane & 7) + ((lane >> 4) << 3);
-        const int c = kk * 2 + ((lane >> 3) & 1);
-        ldsm_x4(b, smem_u32(sk[buf] + swz(key, c)));
-        mma16816(s[2 * j2], qf[kk], b[0], b[1]);
-        mma16816(s[2 * j2 + 1], qf[kk], b[2], b[3]);
-      }
-    }
-    // mask keys beyond Nk
-    const int kbase = t * kBlkK;
-    if (kbase + kBlkK > p.Nk) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c0 = kbase + j * 8 + (lane & 3) * 2;
-        if (c0 >= p.Nk) s[j][0] = s[j][2] = -INFINITY;
-        if (c0 + 1 >= p.Nk) s[j][1] = s[j][3] = -INFINITY;
-      }
-    }
-    // online softmax (rows g and g+8 of the warp's 16)
-    float mx0 = m0, mx1 = m1;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]) * p.scale_log2);
-      mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]) * p.scale_log2);
-    }
-#pragma unroll
-    for (int off = 1; off <= 2; off <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-    }
-    const float a0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - mx0);
-    const float a1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - mx1);
-    const float mb0 = (mx0 == -INFINITY) ? 0.f : mx0;
-    const float mb1 = (mx1 == -INFINITY) ? 0.f : mx1;
-    m0 = mx0;
-    m1 = mx1;
-    float rs0 = 0.f, rs1 = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      s[j][0] = exp2f(s[j][0] * p.scale_log2 - mb0);
-      s[j][1] = exp2f(s[j][1] * p.scale_log2 - mb0);
-      s[j][2] = exp2f(s[j][2] * p.scale_log2 - mb1);
-      s[j][3] = exp2f(s[j][3] * p.scale_log2 - mb1);
-      rs0 += s[j][0] + s[j][1];
-      rs1 += s[j][2] + s[j][3];
-    }
-    l0 = l0 * a0 + rs0;
-    l1 = l1 * a1 + rs1;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      o[i][0] *= a0;
-      o[i][1] *= a0;
-      o[i][2] *= a1;
-      o[i][3] *= a1;
-    }
-    // O += P V
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t pa[4];
-      pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
-      pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
-      pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-#pragma unroll
-      for (int i2 = 0; i2 < 4; ++i2) {
-        // V^T fragments: keys kk*16.., d columns i2*16.. ; trans load
-        uint32_t b[4];
-        const int key = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
-        const int c = i2 * 2 + (lane >> 4);
-        ldsm_x4_t(b, smem_u32(sv[buf] + swz(key, c)));
-        mma16816(o[2 * i2], pa, b[0], b[1]);
-        mma16816(o[2 * i2 + 1], pa, b[2], b[3]);
-      }
-    }
+    if (t == 0) fwd_init(st, sq, warp, lane);
+    fwd_tile(st, sk[buf], sv[buf], t * kBlkK, p.Nk, p.scale_log2, lane);
     __syncthreads();
   }
-  // finalize
-#pragma unroll
-  for (int off = 1; off <= 2; off <<= 1) {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-  }
-  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
-  const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
-  const int r0 = q0 + warp * 16 + (lane >> 2);
-  const int r1 = r0 + 8;
-  __nv_bfloat16* ob = p.o + p.lo.offset(bh, 0);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int c = i * 8 + (lane & 3) * 2;
-    if (c < p.d_valid) {
-      if (r0 < p.Nq)
-        *reinterpret_cast<uint32_t*>(ob + static_cast<int64_t>(r0) * p.lo.row + c) =
-            pack_bf16x2(o[i][0] * inv0, o[i][1] * inv0);
-      if (r1 < p.Nq)
-        *reinterpret_cast<uint32_t*>(ob + static_cast<int64_t>(r1) * p.lo.row + c) =
-            pack_bf16x2(o[i][2] * inv1, o[i][3] * inv1);
+  fwd_store(st, p.o + p.lo.offset(bh, 0), p.lo.row, p.lse, bh, q0, p.Nq, p.d_valid, warp, lane);
+}
+
+// ---------------------------------------------------------------- int8 K/V forward
+// K / V stored int8 with one fp32 scale per (row, head); tiles are dequantized on the
+// way into shared memory (each thread: 8 int8 -> 8 bf16), so no bf16 copy of the
+// cache exists in global memory.
+struct AttnQ8Params {
+  const __nv_bfloat16* q;
+  const int8_t* k;
+  const int8_t* v;
+  const float* ks;
+  const float* vs;
+  __nv_bfloat16* o;
+  float* lse;
+  Layout3 lq, lkv, ls, lo;
+  int BH, Nq, Nk, d_valid;
+  int n_tiles_q;
+  float scale_log2;
+};
+
+__device__ __forceinline__ void load_tile_q8(uint8_t* tile, const int8_t* base, const float* sbase, int64_t row_stride,
+                                             int64_t srow, int row0, int n_valid, int d_valid, int tid, int nthreads) {
+  for (int i = tid; i < 64 * 8; i += nthreads) {
+    const int r = i >> 3, c = i & 7;
+    const int gr = row0 + r;
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    if (gr < n_valid && c * 8 < d_valid) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(base + static_cast<int64_t>(gr) * row_stride + c * 8);
+      const float sc = sbase[static_cast<int64_t>(gr) * srow];
+      const uint32_t lo = raw.x, hi = raw.y;
+      auto cvt = [&](uint32_t word, int byte) -> float {
+        return static_cast<float>(static_cast<int8_t>((word >> (8 * byte)) & 0xFFu)) * sc;
+      };
+      w.x = pack_bf16x2(cvt(lo, 0), cvt(lo, 1));
+      w.y = pack_bf16x2(cvt(lo, 2), cvt(lo, 3));
+      w.z = pack_bf16x2(cvt(hi, 0), cvt(hi, 1));
+      w.w = pack_bf16x2(cvt(hi, 2), cvt(hi, 3));
     }
+    *reinterpret_cast<uint4*>(tile + swz(r, c)) = w;
   }
-  if (p.lse != nullptr && (lane & 3) == 0) {
-    constexpr float kLn2 = 0.6931471805599453f;
-    if (r0 < p.Nq) p.lse[bh * p.Nq + r0] = l0 > 0.f ? (m0 + log2f(l0)) * kLn2 : -INFINITY;
-    if (r1 < p.Nq) p.lse[bh * p.Nq + r1] = l1 > 0.f ? (m1 + log2f(l1)) * kLn2 : -INFINITY;
+}
+
+__global__ void __launch_bounds__(kAttnThreads) attn_fwd_q8_kernel(AttnQ8Params p) {
+  __shared__ __align__(128) uint8_t sq[kBlkQ * 128];
+  __shared__ __align__(128) uint8_t sk[kBlkK * 128];
+  __shared__ __align__(128) uint8_t sv[kBlkK * 128];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t bh = blockIdx.x / p.n_tiles_q;
+  const int q0 = static_cast<int>(blockIdx.x % p.n_tiles_q) * kBlkQ;
+  const __nv_bfloat16* qb = p.q + p.lq.offset(bh, 0);
+  const int8_t* kb = p.k + p.lkv.offset(bh, 0);
+  const int8_t* vb = p.v + p.lkv.offset(bh, 0);
+  const float* ksb = p.ks + p.ls.offset(bh, 0);
+  const float* vsb = p.vs + p.ls.offset(bh, 0);
+  load_tile(sq, qb, p.lq.row, q0, p.Nq, p.d_valid, tid, kAttnThreads);
+  cp_async_commit();
+  cp_async_wait<0>();
+  const int n_tiles = (p.Nk + kBlkK - 1) / kBlkK;
+  FwdState st;
+  for (int t = 0; t < n_tiles; ++t) {
+    load_tile_q8(sk, kb, ksb, p.lkv.row, p.ls.row, t * kBlkK, p.Nk, p.d_valid, tid, kAttnThreads);
+    load_tile_q8(sv, vb, vsb, p.lkv.row, p.ls.row, t * kBlkK, p.Nk, p.d_valid, tid, kAttnThreads);
+    __syncthreads();
+    if (t == 0) fwd_init(st, sq, warp, lane);
+    fwd_tile(st, sk, sv, t * kBlkK, p.Nk, p.scale_log2, lane);
+    __syncthreads();
   }
+  fwd_store(st, p.o + p.lo.offset(bh, 0), p.lo.row, p.lse, bh, q0, p.Nq, p.d_valid, warp, lane);
 }
 
 // ---------------------------------------------------------------- backward
@@ -294,6 +373,7 @@ struct AttnBwdParams {
   __nv_bfloat16* dv;
   Layout3 lq, lk, lv, ldo, ldk, ldv;
   int BH, Nq, Nk, d_valid, q_d_valid;
+  int n_tiles_k;
   float scale, scale_log2;
 };
 
@@ -305,8 +385,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(AttnBwdParams p)
   __shared__ __align__(128) uint8_t sds[kBlkK * 128];  // dS^T [key][q]
   __shared__ float slse[kBlkQ], sdv[kBlkQ];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t bh = blockIdx.y;
-  const int k0 = blockIdx.x * kBlkK;
+  const int64_t bh = blockIdx.x / p.n_tiles_k;
+  const int k0 = static_cast<int>(blockIdx.x % p.n_tiles_k) * kBlkK;
   const __nv_bfloat16* qb = p.q + p.lq.offset(bh, 0);
   const __nv_bfloat16* kb = p.k + p.lk.offset(bh, 0);
   const __nv_bfloat16* vb = p.v + p.lv.offset(bh, 0);
@@ -526,9 +606,54 @@ void attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
   if (BH == 0 || Nq == 0) return;
   TORCH_CHECK(Nk > 0, "attn_fwd: at least one key");
   TORCH_CHECK(BH < 65536 * 32768LL, "attn_fwd: too many heads");
-  dim3 grid(static_cast<unsigned>((Nq + kBlkQ - 1) / kBlkQ), static_cast<unsigned>(BH));
+  p.n_tiles_q = static_cast<int>((Nq + kBlkQ - 1) / kBlkQ);
+  TORCH_CHECK(BH * p.n_tiles_q < 2147483647LL, "attention grid too large");
+  dim3 grid(static_cast<unsigned>(BH * p.n_tiles_q));
   TORCH_CHECK(BH <= 2147483647LL, "attn_fwd: BH too large");
   attn_fwd_kernel<<<grid, kAttnThreads, 0, at::cuda::getCurrentCUDAStream()>>>(p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// kv: int8 [.., 2E] rows (K columns first, V at +E); scales fp32 [.., 2H] (K heads, then V heads).
+void attn_fwd_q8(const torch::Tensor& q, const torch::Tensor& kv, const torch::Tensor& scales, torch::Tensor& o,
+                 const c10::optional<torch::Tensor>& lse, std::vector<int64_t> lq, std::vector<int64_t> lkv,
+                 std::vector<int64_t> ls, std::vector<int64_t> lo, int64_t E, int64_t H, int64_t BH, int64_t Nq,
+                 int64_t Nk, int64_t d_valid, double scale) {
+  check_bf16(q, "q");
+  check_bf16(o, "o");
+  TORCH_CHECK(kv.is_cuda() && kv.scalar_type() == at::kChar, "attn_fwd_q8: int8 K/V");
+  TORCH_CHECK(scales.is_cuda() && scales.scalar_type() == at::kFloat, "attn_fwd_q8: fp32 scales");
+  TORCH_CHECK(d_valid > 0 && d_valid <= kD && d_valid % 8 == 0, "attn_fwd_q8: head dim multiple of 8, <= 64");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(kv.data_ptr()) % 8 == 0, "attn_fwd_q8: 8-byte aligned K/V");
+  const at::cuda::CUDAGuard guard(q.device());
+  if (BH == 0 || Nq == 0) return;
+  TORCH_CHECK(Nk > 0, "attn_fwd_q8: at least one key");
+  AttnQ8Params p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.k = kv.data_ptr<int8_t>();
+  p.v = kv.data_ptr<int8_t>() + E;
+  p.ks = scales.data_ptr<float>();
+  p.vs = scales.data_ptr<float>() + H;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.lq = to_layout(lq);
+  p.lkv = to_layout(lkv);
+  p.ls = to_layout(ls);
+  p.lo = to_layout(lo);
+  TORCH_CHECK(p.lkv.row % 8 == 0 && p.lkv.s0 % 8 == 0 && p.lkv.s1 % 8 == 0 && p.lkv.s2 % 8 == 0,
+              "attn_fwd_q8: K/V rows must be 8-byte aligned");
+  p.BH = static_cast<int>(BH);
+  p.Nq = static_cast<int>(Nq);
+  p.Nk = static_cast<int>(Nk);
+  p.d_valid = static_cast<int>(d_valid);
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  if (lse.has_value() && lse->defined()) {
+    TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->numel() >= BH * Nq, "attn_fwd_q8: fp32 lse [BH, Nq]");
+    p.lse = lse->data_ptr<float>();
+  }
+  p.n_tiles_q = static_cast<int>((Nq + kBlkQ - 1) / kBlkQ);
+  TORCH_CHECK(BH * p.n_tiles_q < 2147483647LL, "attention grid too large");
+  dim3 grid(static_cast<unsigned>(BH * p.n_tiles_q));
+  attn_fwd_q8_kernel<<<grid, kAttnThreads, 0, at::cuda::getCurrentCUDAStream()>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -577,7 +702,9 @@ void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
   p.q_d_valid = p.d_valid;
   p.scale = static_cast<float>(scale);
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
-  dim3 grid(static_cast<unsigned>((Nk + kBlkK - 1) / kBlkK), static_cast<unsigned>(BH));
+  p.n_tiles_k = static_cast<int>((Nk + kBlkK - 1) / kBlkK);
+  TORCH_CHECK(BH * p.n_tiles_k < 2147483647LL, "attention grid too large");
+  dim3 grid(static_cast<unsigned>(BH * p.n_tiles_k));
   attn_bwd_kernel<<<grid, kAttnThreads, 0, stream>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -44,6 +44,7 @@ constexpr uint32_t kTmemCols = 512;  // S[2] (2 x 128) + O[2] (2 x 64) -> 384 us
 
 struct AttnTcParams {
   int Nq, Nk, d_valid;
+  int n_tiles_q;
   float scale_log2;
   // coordinate positions (inside the 5-D maps) of row / i2 / i1 / i0 for Q and for K/V
   int q_pos[4], kv_pos[4];
@@ -84,8 +85,8 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int64_t bh = blockIdx.y;
-  const int q0 = blockIdx.x * kM;
+  const int64_t bh = blockIdx.x / p.n_tiles_q;
+  const int q0 = static_cast<int>(blockIdx.x % p.n_tiles_q) * kM;
   const int i2 = static_cast<int>(bh % p.d2);
   const int i1 = static_cast<int>((bh / p.d2) % p.d1);
   const int i0 = static_cast<int>(bh / (static_cast<int64_t>(p.d1) * p.d2));
@@ -378,8 +379,10 @@ void attn_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
     C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::kSmemBytes));
     configured[dev] = true;
   }
-  TORCH_CHECK(BH <= 65535LL * 65535LL, "attn_fwd_tc: too many heads");
-  dim3 grid(static_cast<unsigned>((Nq + fa::kM - 1) / fa::kM), static_cast<unsigned>(BH));
+  TORCH_CHECK(BH <= 2147483647LL, "attn_fwd_tc: too many heads");
+  p.n_tiles_q = static_cast<int>((Nq + fa::kM - 1) / fa::kM);
+  TORCH_CHECK(BH * p.n_tiles_q < 2147483647LL, "attention grid too large");
+  dim3 grid(static_cast<unsigned>(BH * p.n_tiles_q));
   attn_fwd_tc_kernel<<<grid, fa::kThreads, fa::kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(mq.map, mk.map, mv.map, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -17,6 +17,7 @@ __all__ = [
     "attention_fwd",
     "attention_bwd",
     "attention_fwd_tc",
+    "attention_fwd_q8",
     "rms_scale",
     "rms_apply",
     "rms_bwd",
@@ -101,6 +102,17 @@ def attention_fwd_tc(q, k, v, o, *, lq, lk, lv, lo, BH, Nq, Nk, d, scale, lse=No
     same layout convention as ``attention_fwd``."""
     _lib().attn_fwd_tc(q, k, v, o, lse, _layout(lq), _layout(lk), _layout(lv), _layout(lo), int(BH), int(Nq), int(Nk),
                        int(d), float(scale), status_word(q.device))
+    return o
+
+
+def attention_fwd_q8(q, kv, scales, o, *, lq, lkv, lscale, lo, BH, Nq, Nk, d, scale, lse=None):
+    """Flash attention forward over an int8 K/V cache. ``kv`` is int8 ``[.., 2E]`` (K
+    columns, then V), ``scales`` fp32 ``[.., 2H]``; ``lkv`` / ``lscale`` give the K (and
+    K-scale) layouts, V and its scales sit at +E / +H."""
+    E = kv.shape[-1] // 2
+    H = scales.shape[-1] // 2
+    _lib().attn_fwd_q8(q, kv, scales, o, lse, _layout(lq), _layout(lkv), _layout(lscale), _layout(lo), int(E), int(H),
+                       int(BH), int(Nq), int(Nk), int(d), float(scale))
     return o
 
 

@@ -86,3 +86,47 @@ def test_trainer_reduces_loss_on_fixed_batch():
     losses = [tr.train_step(b.x, b.y, b.eval_pos).item() for _ in range(12)]
     assert all(torch.isfinite(torch.tensor(losses)))
     assert losses[-1] < losses[0]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "int8"])
+def test_native_context_cache_matches_full_forward(dtype):
+    m = _model("nori-tiny").eval()
+    x, y, ep = _data(B=1, S=150, F=7, ep=110)
+    m.impl = "torch"
+    with torch.no_grad():
+        ref = m(x, y[:, :ep], ep, task_type="reg").float()
+    m.impl = "auto"
+    with torch.no_grad():
+        cache = m.build_context_cache(x[:, :ep], y[:, :ep], cache_dtype=dtype)
+        from synthefy_nori_b200.ops.fused_layer import NativeKV
+
+        assert isinstance(cache.caches[0]["seq_kv"], NativeKV)
+        assert cache.caches[0]["seq_kv"].quantized == (dtype == "int8")
+        out = m.apply_context_cache(x[:, ep:], cache, row_chunk_size=17).float()
+    assert _cos(out, ref) > 0.998
+    assert (out - ref).abs().max().item() < 0.08 * ref.abs().max().item() + 0.05
+
+
+def test_int8_attention_kernel_matches_dequantized():
+    import math
+
+    from synthefy_nori_b200 import ops
+
+    torch.manual_seed(7)
+    B, N, T, H, D, nq = 1, 300, 3, 2, 56, 40
+    E = H * D
+    kv = torch.randn(B * N * T, 2 * E, device="cuda")
+    q8, s = ops.quantize_int8(kv.view(-1, 2, H, D))
+    q8, s = q8.view(-1, 2 * E), s.view(-1, 2 * H)
+    deq = (q8.view(-1, 2, H, D).float() * s.view(-1, 2, H, 1)).view(-1, 2 * E).to(torch.bfloat16)
+    q = torch.randn(B * nq * T, E, device="cuda").to(torch.bfloat16)
+    o8 = torch.empty_like(q)
+    ob = torch.empty_like(q)
+    lq = (nq * T * E, E, D, T * E, T, H)
+    l2 = (N * T * 2 * E, 2 * E, D, T * 2 * E, T, H)
+    ls = (N * T * 2 * H, 2 * H, 1, T * 2 * H, T, H)
+    ops.attention_fwd_q8(q, q8, s, o8, lq=lq, lkv=l2, lscale=ls, lo=lq, BH=B * T * H, Nq=nq, Nk=N, d=D,
+                         scale=1 / math.sqrt(D))
+    ops.attention_fwd(q, deq[:, :E], deq[:, E:], ob, lq=lq, lk=l2, lv=l2, lo=lq, BH=B * T * H, Nq=nq, Nk=N, d=D,
+                      scale=1 / math.sqrt(D))
+    torch.testing.assert_close(o8.float(), ob.float(), atol=1e-2, rtol=1e-2)
