@@ -34,7 +34,8 @@ namespace fa {
 constexpr int kM = 128;      // query rows per CTA
 constexpr int kN = 128;      // keys per tile
 constexpr int kD = 64;       // padded head dim
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;  // warps 0 (TMA), 1 (MMA), 4..11 (softmax)
+constexpr int kSoftmaxThreads = 256;
 constexpr int kTileBytes = kM * kD * 2;  // 16 KB (Q, K or V tile)
 constexpr int kPBytes = kM * kN * 2;     // 32 KB (P tile: two 64-key panels)
 // smem: Q | K[2] | V[2] | P[2] | barriers
@@ -54,6 +55,19 @@ struct AttnTcParams {
   float* lse;
   int* status;
 };
+
+// 2^x for x <= 0 on the FMA pipe: x = n + f (n = floor x, f in [0, 1)),
+// 2^f ~ c0 + c1 f + c2 f^2 + c3 f^3 (least-squares fit at Chebyshev nodes on [0, 1),
+// max relative error 7.8e-5, well under bf16's 2^-8), 2^n added to the exponent bits.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float n = floorf(x);
+  const float f = x - n;
+  float pl = fmaf(f, 0.07790716737508774f, 0.22623319923877716f);
+  pl = fmaf(pl, f, 0.6957771182060242f);
+  pl = fmaf(pl, f, 0.999927818775177f);
+  return __int_as_float(__float_as_int(pl) + (static_cast<int>(n) << 23));
+}
 
 __device__ __forceinline__ void coords_for(const int (&pos)[4], int row, int i2, int i1, int i0, int (&c)[5]) {
   c[0] = 0;
@@ -81,8 +95,12 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   uint64_t* p_full = bars + 7;    // [2]
   uint64_t* o_full = bars + 9;    // [2]
   uint64_t* o_free = bars + 11;   // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* xbar = bars + 13;     // [2] row-max exchange between the two column halves
+  uint64_t* sbar = bars + 15;     // row-sum exchange at the end
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  __shared__ float red_max[2][2][kM];  // [iteration parity][column half][row]
+  __shared__ float red_sum[2][kM];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int64_t bh = blockIdx.x / p.n_tiles_q;
@@ -100,10 +118,12 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], kSoftmaxThreads);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 128);
+      mbar_init(&o_free[i], kSoftmaxThreads);
+      mbar_init(&xbar[i], kSoftmaxThreads);
     }
+    mbar_init(sbar, kSoftmaxThreads);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -172,26 +192,26 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax
+    // Two warps per TMEM lane quarter: `half` selects score columns [64 half, 64 half + 64)
+    // (= P panel `half`) and output columns [32 half, 32 half + 32).
     const int q = warp & 3;
+    const int half = (warp - 4) >> 2;
     const int r = q * 32 + lane;  // row in tile == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    float m_prev = -INFINITY, m_cur = -INFINITY, l = 0.f;
-    float o[kD];
+    float m_cur = -INFINITY, l = 0.f;
+    float o[32];
 #pragma unroll
-    for (int i = 0; i < kD; ++i) o[i] = 0.f;
+    for (int i = 0; i < 32; ++i) o[i] = 0.f;
     bool ok = true;
     auto absorb = [&](int j, float a) -> bool {
       const int s = j & 1;
       if (!mbar_wait(&o_full[s], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) return false;
       tc_fence_after();
       uint32_t v[32];
+      tmem_ld32(tO + s * kD + lane_off + half * 32, v);
+      tmem_wait_ld();
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        tmem_ld32(tO + s * kD + lane_off + h * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[h * 32 + i] = o[h * 32 + i] * a + __uint_as_float(v[i]);
-      }
+      for (int i = 0; i < 32; ++i) o[i] = o[i] * a + __uint_as_float(v[i]);
       tc_fence_before();
       mbar_arrive(&o_free[s]);
       return true;
@@ -204,43 +224,45 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int valid = min(kN, p.Nk - j * kN);
-      const uint32_t ts = tS + s * kN + lane_off;
-      // pass 1: row max
+      const int valid = min(kN, p.Nk - j * kN) - half * 64;  // valid columns of this half
+      const uint32_t ts = tS + s * kN + lane_off + half * 64;
+      uint32_t v0[32], v1[32];
+      tmem_ld32(ts, v0);
+      tmem_ld32(ts + 32, v1);
+      tmem_wait_ld();
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(ts + c * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(v[i]));
+      for (int i = 0; i < 32; ++i) {
+        if (i < valid) mx = fmaxf(mx, __uint_as_float(v0[i]));
+        if (32 + i < valid) mx = fmaxf(mx, __uint_as_float(v1[i]));
       }
+      red_max[j & 1][half][r] = mx;
+      mbar_arrive(&xbar[j & 1]);
+      if (!mbar_wait(&xbar[j & 1], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, red_max[j & 1][half ^ 1][r]);
       const float m_new = fmaxf(m_cur, mx * p.scale_log2);
       const float a = exp2f(m_cur - m_new);  // m_cur = -inf on the first tile -> 0
-      // pass 2: P = exp2(s * scale - m), row sum, bf16 P into swizzled smem
       float rsum = 0.f;
-      uint8_t* prow = sP + s * kPBytes;
+      uint8_t* panel = sP + s * kPBytes + half * (kM * 128);
 #pragma unroll
-      for (int c = 0; c < kN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(ts + c * 32, v);
-        tmem_wait_ld();
+      for (int c = 0; c < 2; ++c) {
+        const uint32_t(&v)[32] = c == 0 ? v0 : v1;
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int col = c * 32 + 2 * i;
+          // even columns on the MUFU, odd columns on the FMA pipe (polynomial 2^x)
           const float e0 = col < valid ? exp2f(__uint_as_float(v[2 * i]) * p.scale_log2 - m_new) : 0.f;
-          const float e1 = col + 1 < valid ? exp2f(__uint_as_float(v[2 * i + 1]) * p.scale_log2 - m_new) : 0.f;
+          const float e1 = col + 1 < valid ? exp2_poly(__uint_as_float(v[2 * i + 1]) * p.scale_log2 - m_new) : 0.f;
           pk[i] = pack_bf16x2(e0, e1);
           rsum += bf16lo(pk[i]) + bf16hi(pk[i]);
         }
-        // 32 keys = 4 chunks of 16 bytes in panel (c >> 1), chunks (c & 1) * 4 ..
-        uint8_t* panel = prow + (c >> 1) * (kM * 128);
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
-          const int chunk = (c & 1) * 4 + cc;
+          const int chunk = c * 4 + cc;
           *reinterpret_cast<uint4*>(panel + r * 128 + ((chunk ^ (r & 7)) << 4)) =
               make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
         }
@@ -249,28 +271,27 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[s]);
-      // absorb the previous tile's P V (scaled to the max of that tile)
-      if (j >= 1) {
-        if (!absorb(j - 1, alpha_pending)) {
-          ok = false;
-          break;
-        }
+      if (j >= 1 && !absorb(j - 1, alpha_pending)) {
+        ok = false;
+        break;
       }
-      alpha_pending = a;  // O (relative to m_{j-1}) -> relative to m_j when tile j is absorbed
-      m_prev = m_cur;
+      alpha_pending = a;
       m_cur = m_new;
     }
     if (ok && n_tiles > 0) ok = absorb(n_tiles - 1, alpha_pending);
-    (void)m_prev;
+    red_sum[half][r] = l;
+    mbar_arrive(sbar);
+    if (ok) ok = mbar_wait(sbar, 0, p.status, kTimeoutEpilogue, abort_flag);
     if (ok) {
+      const float lt = red_sum[0][r] + red_sum[1][r];
       const int row = q0 + r;
       if (row < p.Nq) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
         __nv_bfloat16* out = p.o + static_cast<int64_t>(i0) * p.o_s0 + static_cast<int64_t>(i1) * p.o_s1 +
-                             static_cast<int64_t>(i2) * p.o_s2 + static_cast<int64_t>(row) * p.o_row;
+                             static_cast<int64_t>(i2) * p.o_s2 + static_cast<int64_t>(row) * p.o_row + half * 32;
 #pragma unroll
-        for (int c8 = 0; c8 < kD / 8; ++c8) {
-          if (c8 * 8 < p.d_valid) {
+        for (int c8 = 0; c8 < 4; ++c8) {
+          if (half * 32 + c8 * 8 < p.d_valid) {
             *reinterpret_cast<uint4*>(out + c8 * 8) =
                 make_uint4(pack_bf16x2(o[c8 * 8] * inv, o[c8 * 8 + 1] * inv),
                            pack_bf16x2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv),
@@ -278,9 +299,9 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
                            pack_bf16x2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv));
           }
         }
-        if (p.lse != nullptr) {
+        if (p.lse != nullptr && half == 0) {
           constexpr float kLn2 = 0.6931471805599453f;
-          p.lse[bh * p.Nq + row] = l > 0.f ? (m_cur + log2f(l)) * kLn2 : -INFINITY;
+          p.lse[bh * p.Nq + row] = lt > 0.f ? (m_cur + log2f(lt)) * kLn2 : -INFINITY;
         }
       }
     }

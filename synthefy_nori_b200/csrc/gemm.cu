@@ -93,7 +93,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
   uint64_t* rbar = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 1);
+  uint64_t* ebar = rbar + 1;  // [2] bounded epilogue-group barriers (staging free / staging written)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -115,6 +116,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tempty[i], kEpiThreads);
     }
     mbar_init(rbar, 1);
+    mbar_init(&ebar[0], kEpiThreads);
+    mbar_init(&ebar[1], kEpiThreads);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -234,7 +237,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int half = (warp - 2) >> 2;  // column half (32-column chunks alternate)
     const int r_in = q * 32 + lane;  // row inside the tile
     int acc = 0;
-    uint32_t acc_phase = 0, r_phase = 0;
+    uint32_t acc_phase = 0, r_phase = 0, e_phase = 0;
     for (int t = blockIdx.x; t < items; t += gridDim.x) {
       int mb, nb, ks;
       decode(t, mb, nb, ks);
@@ -248,7 +251,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int j = 0; j < BN / kBoxCols; ++j) tma_load_2d(staging + j * kBoxBytes, &tmR, rbar, n0 + j * kBoxCols, m0);
           }
         }
-        named_barrier(1, kEpiThreads);
+        mbar_arrive(&ebar[0]);
+        if (!mbar_wait(&ebar[0], e_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
       }
       if (!mbar_wait(&tfull[acc], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
       if constexpr (EPI == kResidual) {
@@ -335,7 +339,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (acc == 0) acc_phase ^= 1;
       if constexpr (EPI != kF32Atomic) {
         fence_proxy_async_smem();
-        named_barrier(1, kEpiThreads);
+        mbar_arrive(&ebar[1]);
+        if (!mbar_wait(&ebar[1], e_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
+        e_phase ^= 1;
         if (e_tid == 0) {
           const int n0_out = (EPI == kSwiGLU) ? n0 / 2 : n0;
 #pragma unroll

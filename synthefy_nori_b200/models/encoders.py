@@ -365,7 +365,16 @@ class RBFembedding(nn.Module):
         if self.gate_mlp is not None:
             g, b = self.control_table()
             idx = (xw < 0).long() * (2 * self.max_exp + 1) + (e + self.max_exp)
-            rbf = rbf * g[idx] + b[idx]
+            # Select each cell's (gamma, beta) row with a one-hot product rather than a gather:
+            # the values are identical (exact fp32 selection), but the backward pass becomes
+            # one small GEMM instead of millions of contended index-accumulations into a
+            # 38-row table.
+            gb = torch.cat((g, b), -1)
+            oh = torch.nn.functional.one_hot(idx, gb.shape[0]).to(gb.dtype)
+            with torch.autocast(device_type=x.device.type, enabled=False):
+                sel = oh @ gb
+            gs, bs = sel.split(self.n_kernels, -1)
+            rbf = rbf * gs + bs
             rbf = self.norm(rbf)
         if self.use_original_features:
             rbf = torch.cat([rbf, x.unsqueeze(-1).to(rbf.dtype)], -1)

@@ -259,6 +259,14 @@ class FeaturesTransformer(nn.Module):
             self.feature_positional_embedding = nn.Linear(embed_dim // 4, embed_dim)
         self.x_preprocess = build_x_preprocess(**preprocess_config_x)
 
+    def load_state_dict(self, state_dict, strict: bool = True, assign: bool = False):
+        """Load weights and invalidate the native path's cached bf16 weight layouts."""
+        result = super().load_state_dict(state_dict, strict=strict, assign=assign)
+        from synthefy_nori_b200.ops.fused_layer import bump_weight_generation
+
+        bump_weight_generation()
+        return result
+
     # ------------------------------------------------------------------ dispatch
     def use_native(self, device: torch.device) -> bool:
         if self.impl == "torch":

@@ -116,11 +116,15 @@ def attention_fwd_q8(q, kv, scales, o, *, lq, lkv, lscale, lo, BH, Nq, Nk, d, sc
     return o
 
 
-def attention_bwd(q, k, v, o, do, lse, dq_f32, dk, dv, *, lq, lk, lv, lo, ldo, ldk, ldv, BH, Nq, Nk, d, scale):
-    """Flash attention backward. ``dq_f32`` is a zeroed fp32 [BH, Nq, 64] accumulator
-    (scaled dQ); dK / dV are written through their layouts."""
+def attention_bwd(q, k, v, o, do, lse, dq_f32, dk, dv, *, lq, lk, lv, lo, ldo, ldk, ldv, BH, Nq, Nk, d, scale,
+                  ldq=None):
+    """Flash attention backward. ``dq_f32`` is a zeroed fp32 accumulator addressed through
+    ``ldq`` (default: head-major ``[BH, Nq, 64]``); dK / dV are written through their layouts."""
+    if ldq is None:
+        ldq = (Nq * 64, 0, 0, 64, 1, 1)
     _lib().attn_bwd(q, k, v, o, do, lse, dq_f32, dk, dv, _layout(lq), _layout(lk), _layout(lv), _layout(lo),
-                    _layout(ldo), _layout(ldk), _layout(ldv), int(BH), int(Nq), int(Nk), int(d), float(scale))
+                    _layout(ldo), _layout(ldk), _layout(ldv), _layout(ldq), int(BH), int(Nq), int(Nk), int(d),
+                    float(scale))
 
 
 def rms_scale(x: torch.Tensor, eps: float) -> torch.Tensor:

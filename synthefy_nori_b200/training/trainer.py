@@ -88,4 +88,7 @@ class NoriTrainer:
                 dist.all_reduce(self.flat.grad, group=self.pg)
             scale = 1.0 / self.world
         self.opt.step(grad_scale=scale)
+        from synthefy_nori_b200.ops.fused_layer import bump_weight_generation
+
+        bump_weight_generation()
         return loss.detach()
