@@ -113,11 +113,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], kEpiThreads);
+      mbar_init(&tempty[i], kEpiThreads / 32);
     }
     mbar_init(rbar, 1);
-    mbar_init(&ebar[0], kEpiThreads);
-    mbar_init(&ebar[1], kEpiThreads);
+    mbar_init(&ebar[0], kEpiThreads / 32);
+    mbar_init(&ebar[1], kEpiThreads / 32);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -251,12 +251,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int j = 0; j < BN / kBoxCols; ++j) tma_load_2d(staging + j * kBoxBytes, &tmR, rbar, n0 + j * kBoxCols, m0);
           }
         }
-        mbar_arrive(&ebar[0]);
-        if (!mbar_wait(&ebar[0], e_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ebar[0]);
+        if (!mbar_wait_warp(&ebar[0], e_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
       }
-      if (!mbar_wait(&tfull[acc], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
       if constexpr (EPI == kResidual) {
-        if (!mbar_wait(rbar, r_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
+        if (!mbar_wait_warp(rbar, r_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
         r_phase ^= 1;
       }
       tc_fence_after();
@@ -334,13 +335,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (p.sumsq != nullptr && row_ok) atomicAdd(&p.sumsq[row], ssq);
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
       if constexpr (EPI != kF32Atomic) {
         fence_proxy_async_smem();
-        mbar_arrive(&ebar[1]);
-        if (!mbar_wait(&ebar[1], e_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ebar[1]);
+        if (!mbar_wait_warp(&ebar[1], e_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
         e_phase ^= 1;
         if (e_tid == 0) {
           const int n0_out = (EPI == kSwiGLU) ? n0 / 2 : n0;

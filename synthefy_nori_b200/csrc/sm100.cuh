@@ -92,6 +92,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// Warp-collective bounded wait: every lane polls, and the outcome is made uniform across
+// the warp (if any lane gave up, all lanes report failure), so warp-synchronous code after
+// the wait never diverges.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code,
+                                               volatile int* abort) {
+  const bool ok = mbar_wait(bar, parity, status, code, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ------------------------------------------------------------------ TMA (no multicast)
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

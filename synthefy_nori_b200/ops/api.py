@@ -30,6 +30,8 @@ __all__ = [
     "status_word",
     "check_status",
     "interleave_swiglu_weights",
+    "qass_fwd",
+    "qass_bwd",
 ]
 
 _STATUS: dict[int, torch.Tensor] = {}
@@ -170,6 +172,17 @@ def quantize_int8(x: torch.Tensor):
     """Per-row (last dim) absmax int8: returns (q int8, scale fp32 with last dim 1)."""
     q, s = _lib().quantize_int8(x.contiguous())
     return q, s
+
+
+def qass_fwd(q, s, w1=None, b1=None, w2=None, b2=None, *, H: int, D: int):
+    """``q * s * (1 + tanh(W2 gelu(W1 q + b1) + b2))`` per head vector (gate optional)."""
+    return _lib().qass_fwd(q, s, w1, b1, w2, b2, int(H), int(D))
+
+
+def qass_bwd(q, dout, s, gs, w1=None, b1=None, w2=None, b2=None, gw1=None, gb1=None, gw2=None, gb2=None, *, H: int,
+             D: int):
+    """Backward of ``qass_fwd``: returns dq (bf16); accumulates ds and the gate-MLP grads."""
+    return _lib().qass_bwd(q, dout, s, w1, b1, w2, b2, gs, gw1, gb1, gw2, gb2, int(H), int(D))
 
 
 def interleave_swiglu_weights(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
