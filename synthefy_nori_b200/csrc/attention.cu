@@ -711,3 +711,104 @@ void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
 }
 
 }  // namespace nori
+
+// ---------------------------------------------------------------- allocation-free variant
+// See nori_noalloc.h. The scratch for the dO . O row products lives in this file-scope
+// device array; host code must not pass `g_noalloc_dvec` itself to a kernel (on the host
+// it names a host-side shadow), only the address returned by cudaGetSymbolAddress.
+#include <mutex>
+#include <string>
+
+#include "nori_noalloc.h"
+
+namespace {
+static __device__ __align__(256) float g_noalloc_dvec[NORI_NOALLOC_MAX_ROWS];
+
+constexpr int kMaxDevices = 64;
+float* g_noalloc_addr[kMaxDevices] = {nullptr};
+std::mutex g_noalloc_mutex;
+thread_local std::string g_noalloc_error;
+
+cudaError_t noalloc_fail(const char* why) {
+  g_noalloc_error = why;
+  return cudaErrorInvalidValue;
+}
+
+nori::Layout3 layout_from(const int64_t* l) {
+  return nori::Layout3{l[0], l[1], l[2], l[3], static_cast<int>(l[4]), static_cast<int>(l[5])};
+}
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) const char* nori_attention_bwd_noalloc_error(void) {
+  return g_noalloc_error.c_str();
+}
+
+extern "C" __attribute__((visibility("default"))) cudaError_t nori_attention_bwd_noalloc(
+    const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse, float* dq, void* dk,
+    void* dv, const int64_t* lq, const int64_t* lk, const int64_t* lv, const int64_t* lo, const int64_t* ldo,
+    const int64_t* ldk, const int64_t* ldv, int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid, double scale,
+    cudaStream_t stream) {
+  g_noalloc_error.clear();
+  if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv || !lq || !lk || !lv || !lo || !ldo || !ldk || !ldv)
+    return noalloc_fail("nori_attention_bwd_noalloc: null pointer argument");
+  if (BH < 0 || Nq < 0 || Nk < 0) return noalloc_fail("nori_attention_bwd_noalloc: negative size");
+  if (BH * Nq > static_cast<int64_t>(NORI_NOALLOC_MAX_ROWS))
+    return noalloc_fail("nori_attention_bwd_noalloc: BH * Nq exceeds NORI_NOALLOC_MAX_ROWS (1048576)");
+  if (d_valid <= 0 || d_valid > nori::kD || d_valid % 8 != 0)
+    return noalloc_fail("nori_attention_bwd_noalloc: head dim must be a multiple of 8, at most 64");
+  if (BH == 0 || Nq == 0 || Nk == 0) return cudaSuccess;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= kMaxDevices) return noalloc_fail("nori_attention_bwd_noalloc: device index out of range");
+  float* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_addr[dev] == nullptr) {
+      // once per device, with that device current
+      err = cudaGetSymbolAddress(reinterpret_cast<void**>(&g_noalloc_addr[dev]), g_noalloc_dvec);
+      if (err != cudaSuccess) {
+        g_noalloc_addr[dev] = nullptr;
+        return err;
+      }
+    }
+    scratch = g_noalloc_addr[dev];
+  }
+  // the query-gradient accumulator must start at zero
+  err = cudaMemsetAsync(dq, 0, static_cast<size_t>(BH * Nq * nori::kD) * sizeof(float), stream);
+  if (err != cudaSuccess) return err;
+  const int64_t rows = BH * Nq;
+  nori::attn_bwd_dot_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(dout), layout_from(lo),
+      layout_from(ldo), static_cast<int>(BH), static_cast<int>(Nq), static_cast<int>(d_valid), scratch);
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return err;
+  nori::AttnBwdParams p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  p.k = reinterpret_cast<const __nv_bfloat16*>(k);
+  p.v = reinterpret_cast<const __nv_bfloat16*>(v);
+  p.dout = reinterpret_cast<const __nv_bfloat16*>(dout);
+  p.lse = lse;
+  p.dvec = scratch;
+  p.dq = dq;
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk);
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv);
+  p.lq = layout_from(lq);
+  p.lk = layout_from(lk);
+  p.lv = layout_from(lv);
+  p.ldo = layout_from(ldo);
+  p.ldk = layout_from(ldk);
+  p.ldv = layout_from(ldv);
+  p.ldq = nori::Layout3{Nq * nori::kD, 0, 0, nori::kD, 1, 1};
+  p.BH = static_cast<int>(BH);
+  p.Nq = static_cast<int>(Nq);
+  p.Nk = static_cast<int>(Nk);
+  p.d_valid = static_cast<int>(d_valid);
+  p.q_d_valid = p.d_valid;
+  p.scale = static_cast<float>(scale);
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  p.n_tiles_k = static_cast<int>((Nk + nori::kBlkK - 1) / nori::kBlkK);
+  if (BH * p.n_tiles_k >= 2147483647LL) return noalloc_fail("nori_attention_bwd_noalloc: grid too large");
+  nori::attn_bwd_kernel<<<static_cast<unsigned>(BH * p.n_tiles_k), nori::kAttnThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
