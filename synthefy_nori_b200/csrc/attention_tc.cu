@@ -70,6 +70,14 @@ __device__ __forceinline__ float exp2_poly(float x) {
   return __int_as_float(__float_as_int(pl) + (static_cast<int>(n) << 23));
 }
 
+// 2^x on the MUFU (one instruction; flushes subnormal results to zero, which the bf16 P
+// cannot represent anyway).
+__device__ __forceinline__ float exp2_mufu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void coords_for(const int (&pos)[4], int row, int i2, int i1, int i0, int (&c)[5]) {
   c[0] = 0;
   c[pos[0]] = row;
@@ -232,11 +240,17 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
       tmem_ld32(ts, v0);
       tmem_ld32(ts + 32, v1);
       tmem_wait_ld();
+      const bool full_tile = valid >= 64;
       float mx = -INFINITY;
+      if (full_tile) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if (i < valid) mx = fmaxf(mx, __uint_as_float(v0[i]));
-        if (32 + i < valid) mx = fmaxf(mx, __uint_as_float(v1[i]));
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(__uint_as_float(v0[i]), __uint_as_float(v1[i])));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (i < valid) mx = fmaxf(mx, __uint_as_float(v0[i]));
+          if (32 + i < valid) mx = fmaxf(mx, __uint_as_float(v1[i]));
+        }
       }
       red_max[j & 1][half][r] = mx;
       __syncwarp();
@@ -248,20 +262,31 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
       mx = fmaxf(mx, red_max[j & 1][half ^ 1][r]);
       const float m_new = fmaxf(m_cur, mx * p.scale_log2);
       const float a = exp2f(m_cur - m_new);  // m_cur = -inf on the first tile -> 0
+      const float nm = -m_new;
       float rsum = 0.f;
       uint8_t* panel = sP + s * kPBytes + half * (kM * 128);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const uint32_t(&v)[32] = c == 0 ? v0 : v1;
         uint32_t pk[16];
+        if (full_tile) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int col = c * 32 + 2 * i;
-          // even columns on the MUFU, odd columns on the FMA pipe (polynomial 2^x)
-          const float e0 = col < valid ? exp2f(__uint_as_float(v[2 * i]) * p.scale_log2 - m_new) : 0.f;
-          const float e1 = col + 1 < valid ? exp2_poly(__uint_as_float(v[2 * i + 1]) * p.scale_log2 - m_new) : 0.f;
-          pk[i] = pack_bf16x2(e0, e1);
-          rsum += bf16lo(pk[i]) + bf16hi(pk[i]);
+          for (int i = 0; i < 16; ++i) {
+            // even columns on the MUFU, odd columns on the FMA pipe (polynomial 2^x)
+            const float e0 = exp2_mufu(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, nm));
+            const float e1 = exp2_poly(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, nm));
+            pk[i] = pack_bf16x2(e0, e1);
+            rsum += e0 + e1;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int col = c * 32 + 2 * i;
+            const float e0 = col < valid ? exp2_mufu(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, nm)) : 0.f;
+            const float e1 = col + 1 < valid ? exp2_poly(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, nm)) : 0.f;
+            pk[i] = pack_bf16x2(e0, e1);
+            rsum += e0 + e1;
+          }
         }
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
