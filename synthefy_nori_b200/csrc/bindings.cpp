@@ -42,6 +42,18 @@ torch::Tensor qass_bwd(const torch::Tensor& q, const torch::Tensor& dout, const 
                        torch::Tensor& gs, const c10::optional<torch::Tensor>& gw1,
                        const c10::optional<torch::Tensor>& gb1, const c10::optional<torch::Tensor>& gw2,
                        const c10::optional<torch::Tensor>& gb2, int64_t H, int64_t D);
+void peer_ddp_step(std::vector<int64_t> grads, std::vector<int64_t> params, std::vector<int64_t> flags,
+                   std::vector<int64_t> norms, int64_t rank, int64_t s0, int64_t s1, const torch::Tensor& bounds,
+                   int64_t step, torch::Tensor& red, torch::Tensor& m, torch::Tensor& v,
+                   const c10::optional<torch::Tensor>& ema, torch::Tensor& local_norm, double lr, double beta1,
+                   double beta2, double eps, double wd, int64_t opt_step, double ema_decay, double max_norm,
+                   double grad_scale, const torch::Tensor& status);
+int64_t peer_malloc(int64_t bytes);
+void peer_free(int64_t ptr);
+torch::Tensor peer_ipc_handle(int64_t ptr);
+int64_t peer_ipc_open(const torch::Tensor& handle);
+void peer_ipc_close(int64_t ptr);
+torch::Tensor tensor_from_ptr(int64_t ptr, int64_t numel, int64_t device, c10::ScalarType dtype);
 torch::Tensor rms_scale(const torch::Tensor& x, double eps);
 torch::Tensor sumsq_to_scale(const torch::Tensor& ssq, int64_t E, double eps);
 std::vector<torch::Tensor> pinball_fused(const torch::Tensor& pred, const torch::Tensor& target,
@@ -66,6 +78,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd_tc", &nori::attn_fwd_tc);
   m.def("attn_fwd_q8", &nori::attn_fwd_q8);
   m.def("rms_scale", &nori::rms_scale);
+  m.def("peer_ddp_step", &nori::peer_ddp_step);
+  m.def("peer_malloc", &nori::peer_malloc);
+  m.def("peer_free", &nori::peer_free);
+  m.def("peer_ipc_handle", &nori::peer_ipc_handle);
+  m.def("peer_ipc_open", &nori::peer_ipc_open);
+  m.def("peer_ipc_close", &nori::peer_ipc_close);
+  m.def("tensor_from_ptr", &nori::tensor_from_ptr);
   m.def("qass_fwd", &nori::qass_fwd);
   m.def("qass_bwd", &nori::qass_bwd);
   m.def("rms_apply", &nori::rms_apply);

@@ -62,33 +62,45 @@ class NoriTrainer:
         if self.world > 1:
             for p in self.model.parameters():  # identical initial weights on every rank
                 dist.broadcast(p.data, 0, group=process_group)
-        self.flat = FlatParams(self.model.parameters(), device)
-        self.opt = FusedAdamWEMA(self.flat, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps, weight_decay=cfg.weight_decay,
-                                 ema_decay=cfg.ema_decay, max_grad_norm=cfg.max_grad_norm)
-        self.quantiles = torch.tensor(model.regression_quantiles, device=device, dtype=torch.float32)
-        self.reducer = None
+        self.peer = None
         if self.world > 1 and cfg.grad_reduction == "peer":
-            from synthefy_nori_b200.parallel.peer_reduce import PeerGradReducer
+            from synthefy_nori_b200.parallel.peer_reduce import PeerDDP
 
-            self.reducer = PeerGradReducer(self.flat.grad, process_group)
+            self.peer = PeerDDP(self.model.parameters(), device, process_group, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
+                                weight_decay=cfg.weight_decay, ema_decay=cfg.ema_decay,
+                                max_grad_norm=cfg.max_grad_norm)
+            self.flat = self.opt = None
+        else:
+            self.flat = FlatParams(self.model.parameters(), device)
+            self.opt = FusedAdamWEMA(self.flat, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps, weight_decay=cfg.weight_decay,
+                                     ema_decay=cfg.ema_decay, max_grad_norm=cfg.max_grad_norm)
+        self.quantiles = torch.tensor(model.regression_quantiles, device=device, dtype=torch.float32)
 
     def train_step(self, x: torch.Tensor, y: torch.Tensor, eval_pos: int) -> torch.Tensor:
         """One optimizer step on tables ``x [B, N, F]`` with targets ``y [B, N]``.
         Returns the (device) loss."""
-        self.flat.zero_grad()
+        if self.peer is not None:
+            self.peer.zero_grad()
+        else:
+            self.flat.zero_grad()
         pred = forward_native(self.model, x, y[:, :eval_pos], eval_pos, self.cfg.checkpoint_layers)
         loss = pinball_objective(pred, y[:, eval_pos:], self.quantiles, self.cfg.pinball_tail_weight,
                                  self.cfg.pinball_monotonicity_weight, self.cfg.pinball_mse_weight)
         loss.backward()
-        scale = 1.0
-        if self.world > 1:
-            if self.reducer is not None:
-                self.reducer.all_reduce_sum()
-            else:
+        if self.peer is not None:
+            self.peer.step()  # peer-memory reduce-scatter + sharded AdamW/EMA + all-gather
+        else:
+            scale = 1.0
+            if self.world > 1:
                 dist.all_reduce(self.flat.grad, group=self.pg)
-            scale = 1.0 / self.world
-        self.opt.step(grad_scale=scale)
+                scale = 1.0 / self.world
+            self.opt.step(grad_scale=scale)
         from synthefy_nori_b200.ops.fused_layer import bump_weight_generation
 
         bump_weight_generation()
         return loss.detach()
+
+    def close(self) -> None:
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
