@@ -62,6 +62,11 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--grad-reduction", default="nccl", choices=["nccl", "peer"])
+    ap.add_argument("--workload", default="train", choices=["train", "infer5", "infer4"],
+                    help="train (headline), infer5 (batched multi-table cached inference, BASELINE config 5), "
+                         "infer4 (100k-row context, int8 KV, BASELINE config 4)")
+    ap.add_argument("--infer-tables", type=int, default=256)
+    ap.add_argument("--infer-group", type=int, default=8, help="tables per cache build / predict batch")
     return ap.parse_args()
 
 
@@ -287,6 +292,123 @@ def run_reference(args, device, world, rank):
     return ms, clk, 0, None, float(losses[-1].item())
 
 
+# ----------------------------------------------------------------------------- inference
+def _infer_tables(n_tables, n_ctx, n_q, n_feat, seed, device, nan_frac=0.15, n_cat=0):
+    """Synthetic tables: X ~ N(0,1) (optional categorical codes), NaNs, y = random 2-layer MLP(X) + noise."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    N = n_ctx + n_q
+    X = torch.randn(n_tables, N, n_feat, generator=g, device=device)
+    if n_cat:
+        card = torch.randint(2, 51, (n_cat,), generator=g, device=device)
+        X[:, :, :n_cat] = torch.floor(torch.rand(n_tables, N, n_cat, generator=g, device=device) * card)
+    W1 = torch.randn(n_tables, n_feat, 64, generator=g, device=device) / n_feat ** 0.5
+    W2 = torch.randn(n_tables, 64, 1, generator=g, device=device) / 8.0
+    y = torch.bmm(torch.tanh(torch.bmm(X, W1)), W2).squeeze(-1) + 0.05 * torch.randn(n_tables, N, generator=g,
+                                                                                      device=device)
+    X[torch.rand(X.shape, generator=g, device=device) < nan_frac] = float("nan")
+    y = (y - y[:, :n_ctx].mean(1, keepdim=True)) / y[:, :n_ctx].std(1, keepdim=True).clamp_min(1e-6)
+    return X, y
+
+
+def run_infer5(args, device, world, rank, impl):
+    """tables data-parallel over ranks; per group of tables the context
+    cache is built once, then 4 predict calls with 512 fresh query rows each (timed)."""
+    n_ctx, n_feat, n_q, calls = 2048, 50, 512, 4
+    per_rank = args.infer_tables // world
+    grp = args.infer_group
+    if impl == "reference":
+        from synthefy_nori_b200.utils.reference import import_reference
+
+        import_reference()
+        from synthefy_nori.utils.loading import build_model as mk
+    else:
+        from synthefy_nori_b200.utils.loading import build_model as mk
+    from synthefy_nori_b200.models.config import preset_config
+
+    torch.manual_seed(args.seed)
+    model = mk(dict(preset_config(args.model))).to(device).eval()
+    build_ms = pred_ms = 0.0
+    groups = [(i, min(grp, per_rank - i)) for i in range(0, per_rank, grp)]
+    # warm-up on one group
+    warm = groups[: max(1, min(args.warmup, 1))]
+    for phase, gl in (("warm", warm), ("timed", groups)):
+        for gi, (off, n) in enumerate(gl):
+            X, y = _infer_tables(n, n_ctx, n_q * calls, n_feat, args.seed + rank * 100003 + off, device)
+            if world > 1 and phase == "timed":
+                dist.barrier()
+            torch.cuda.synchronize(device)
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record()
+            with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16, enabled=impl == "reference"):
+                cache = model.build_context_cache(X[:, :n_ctx], y[:, :n_ctx], cache_dtype="bf16")
+                e1.record()
+                for c in range(calls):
+                    xq = X[:, n_ctx + c * n_q : n_ctx + (c + 1) * n_q]
+                    model.apply_context_cache(xq, cache)
+            e2.record()
+            torch.cuda.synchronize(device)
+            if phase == "timed":
+                build_ms += e0.elapsed_time(e1)
+                pred_ms += e1.elapsed_time(e2)
+            del cache
+    t = torch.tensor([build_ms, pred_ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    build_ms, pred_ms = float(t[0]), float(t[1])
+    rows = per_rank * world * n_q * calls
+    return {"metric": "nori-100m batched multi-table cached inference query rows/s", "value": rows / (pred_ms / 1000),
+            "unit": "query rows/s", "ms_predict_total": pred_ms, "ms_cache_build_total": build_ms,
+            "tables": per_rank * world, "ctx_rows": n_ctx, "features": n_feat, "query_rows_per_call": n_q,
+            "calls": calls, "group": grp}
+
+
+def run_infer4(args, device, world, rank, impl):
+    """BASELINE config 4 on one GPU: one table, 100k context rows x 100 features (20
+    categorical), int8 KV cache, 10k query rows; build + query timed separately."""
+    n_ctx = int(os.environ.get("NORI_INFER4_CTX", "100000"))
+    n_q = int(os.environ.get("NORI_INFER4_QUERY", "10000"))
+    from synthefy_nori_b200.models.config import preset_config
+
+    if impl == "reference":
+        from synthefy_nori_b200.utils.reference import import_reference
+
+        import_reference()
+        from synthefy_nori.utils.loading import build_model as mk
+    else:
+        from synthefy_nori_b200.utils.loading import build_model as mk
+    torch.manual_seed(args.seed)
+    model = mk(dict(preset_config(args.model))).to(device).eval()
+    X, y = _infer_tables(1, n_ctx, n_q, 100, args.seed, device, nan_frac=0.10, n_cat=20)
+    torch.cuda.synchronize(device)
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record()
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16, enabled=impl == "reference"):
+        if impl == "reference":
+            cache = model.build_context_cache(X[:, :n_ctx], y[:, :n_ctx], cache_dtype="int8")
+        else:
+            cache = model.build_context_cache(X[:, :n_ctx], y[:, :n_ctx], cache_dtype="int8")
+        e1.record()
+        model.apply_context_cache(X[:, n_ctx:], cache, row_chunk_size=2048)
+    e2.record()
+    torch.cuda.synchronize(device)
+    b, q = e0.elapsed_time(e1), e1.elapsed_time(e2)
+    return {"metric": "nori-100m 100k-ctx infer query rows/s", "value": n_q / ((b + q) / 1000), "unit": "query rows/s",
+            "ms_cache_build": b, "ms_query": q, "ctx_rows": n_ctx, "query_rows": n_q, "cache": "int8",
+            "query_rows_per_s_excluding_build": n_q / (q / 1000)}
+
+
+def main_infer(args, device, world, rank):
+    res = run_infer5(args, device, world, rank, args.impl) if args.workload == "infer5" else \
+        run_infer4(args, device, world, rank, args.impl)
+    if rank == 0:
+        res.update({"n_gpus": world, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+                    "config": {"model": args.model, "parallelism": f"tables-dp{world}" if args.workload == "infer5"
+                               else "single-gpu"}})
+        if args.impl == "reference":
+            res["impl"] = "reference"
+        print(json.dumps(res), flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -302,6 +424,12 @@ def main():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
     t0 = time.time()
+    if args.workload != "train":
+        main_infer(args, device, world, rank)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.impl == "reference":
         res = run_reference(args, device, world, rank)
         if res is None:

@@ -54,6 +54,8 @@ torch::Tensor peer_ipc_handle(int64_t ptr);
 int64_t peer_ipc_open(const torch::Tensor& handle);
 void peer_ipc_close(int64_t ptr);
 torch::Tensor tensor_from_ptr(int64_t ptr, int64_t numel, int64_t device, c10::ScalarType dtype);
+std::vector<torch::Tensor> quantile_decode(const torch::Tensor& pred, const torch::Tensor& taus,
+                                           const torch::Tensor& levels, bool return_sorted);
 torch::Tensor rms_scale(const torch::Tensor& x, double eps);
 torch::Tensor sumsq_to_scale(const torch::Tensor& ssq, int64_t E, double eps);
 std::vector<torch::Tensor> pinball_fused(const torch::Tensor& pred, const torch::Tensor& target,
@@ -78,6 +80,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd_tc", &nori::attn_fwd_tc);
   m.def("attn_fwd_q8", &nori::attn_fwd_q8);
   m.def("rms_scale", &nori::rms_scale);
+  m.def("quantile_decode", &nori::quantile_decode);
   m.def("peer_ddp_step", &nori::peer_ddp_step);
   m.def("peer_malloc", &nori::peer_malloc);
   m.def("peer_free", &nori::peer_free);

@@ -31,6 +31,7 @@ __all__ = [
     "check_status",
     "interleave_swiglu_weights",
     "qass_fwd",
+    "quantile_decode",
     "qass_bwd",
 ]
 
@@ -183,6 +184,15 @@ def qass_bwd(q, dout, s, gs, w1=None, b1=None, w2=None, b2=None, gw1=None, gb1=N
              D: int):
     """Backward of ``qass_fwd``: returns dq (bf16); accumulates ds and the gate-MLP grads."""
     return _lib().qass_bwd(q, dout, s, w1, b1, w2, b2, gs, gw1, gb1, gw2, gb2, int(H), int(D))
+
+
+def quantile_decode(pred: torch.Tensor, taus: torch.Tensor, levels=None, return_sorted: bool = False):
+    """Sort each row's quantiles, trapezoid mean, interpolate at ``levels``.
+    Returns (mean [R], quantiles [R, L], sorted [R, K] or empty)."""
+    if levels is None:
+        levels = torch.tensor([0.5], device=pred.device)
+    return _lib().quantile_decode(pred.contiguous(), taus.float().contiguous(), levels.float().contiguous(),
+                                  bool(return_sorted))
 
 
 def interleave_swiglu_weights(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:

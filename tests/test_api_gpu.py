@@ -1,0 +1,39 @@
+"""NoriRegressor on the native CUDA path vs the CPU (PyTorch) path, and the native
+quantile decode vs its PyTorch statement."""
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_quantile_decode_kernel_matches_torch():
+    from synthefy_nori_b200 import ops
+    from synthefy_nori_b200.inference.predictor import decode_torch
+
+    torch.manual_seed(0)
+    taus = torch.tensor([(i + 1) / 1000 for i in range(999)], device="cuda")
+    raw = torch.randn(33, 999, device="cuda")
+    lv = torch.tensor([0.0005, 0.1, 0.5, 0.9, 0.9995], device="cuda")
+    m, q, s = ops.quantile_decode(raw, taus, lv, True)
+    rm, rq, rs = decode_torch(raw, taus, lv, True)
+    torch.testing.assert_close(s, rs)
+    torch.testing.assert_close(m, rm, atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(q, rq, atol=1e-5, rtol=1e-5)
+
+
+def test_regressor_cuda_matches_cpu():
+    from synthefy_nori_b200.api import NoriRegressor
+
+    rng = np.random.default_rng(0)
+    X = rng.standard_normal((140, 6)).astype(np.float32)
+    y = X @ rng.standard_normal(6) + 0.1 * rng.standard_normal(140)
+    kw = dict(model="nori-tiny", weights="random", n_estimators=2)
+    cpu = NoriRegressor(device="cpu", **kw).fit(X[:100], y[:100])
+    gpu = NoriRegressor(device="cuda", **kw).fit(X[:100], y[:100])
+    a, b = cpu.predict(X[100:]), gpu.predict(X[100:])
+    assert np.max(np.abs(a - b)) < 0.05 * np.std(y) + 1e-3
+    qa = cpu.predict(X[100:], output_type="quantiles", quantiles=[0.1, 0.9])
+    qb = gpu.predict(X[100:], output_type="quantiles", quantiles=[0.1, 0.9])
+    assert np.max(np.abs(qa - qb)) < 0.08 * np.std(y) + 1e-3
