@@ -61,7 +61,9 @@ def parse():
     ap.add_argument("--features", type=int, default=100)
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--grad-reduction", default="nccl", choices=["nccl", "peer"])
+    ap.add_argument("--grad-reduction", default="peer", choices=["nccl", "peer"],
+                    help="N > 1: peer = in-kernel reduce-scatter / sharded AdamW / all-gather over NVLink peer memory; "
+                         "nccl = all-reduce baseline")
     ap.add_argument("--workload", default="train", choices=["train", "infer5", "infer4"],
                     help="train (headline), infer5 (batched multi-table cached inference, BASELINE config 5), "
                          "infer4 (100k-row context, int8 KV, BASELINE config 4)")
