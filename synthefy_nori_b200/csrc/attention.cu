@@ -712,6 +712,26 @@ void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
 
 }  // namespace nori
 
+namespace nori {
+// Dvec = rowsum(dO * O) for the tensor-core backward (same kernel as attn_bwd's first step).
+torch::Tensor attn_dvec(const torch::Tensor& o, const torch::Tensor& dout, std::vector<int64_t> lo,
+                        std::vector<int64_t> ldo, int64_t BH, int64_t Nq, int64_t d_valid) {
+  check_bf16(o, "o");
+  check_bf16(dout, "dout");
+  TORCH_CHECK(d_valid > 0 && d_valid <= kD && d_valid % 8 == 0, "attn_dvec: head dim multiple of 8, <= 64");
+  const at::cuda::CUDAGuard guard(o.device());
+  auto dvec = torch::empty({BH * Nq}, o.options().dtype(at::kFloat));
+  if (BH * Nq == 0) return dvec;
+  const int64_t rows = BH * Nq;
+  attn_bwd_dot_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+      to_layout(lo), to_layout(ldo), static_cast<int>(BH), static_cast<int>(Nq), static_cast<int>(d_valid),
+      dvec.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dvec;
+}
+}  // namespace nori
+
 // ---------------------------------------------------------------- allocation-free variant
 // See nori_noalloc.h. The scratch for the dO . O row products lives in this file-scope
 // device array; host code must not pass `g_noalloc_dvec` itself to a kernel (on the host

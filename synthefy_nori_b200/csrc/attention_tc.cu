@@ -345,6 +345,296 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ backward
+// One CTA = 128 keys of one head; loop over 128-row query blocks:
+//   S^T  = K Q^T     (M=128 keys, N=128 q, K=64)   -> TMEM
+//   dP^T = V dO^T    (M=128 keys, N=128 q, K=64)   -> TMEM
+//   softmax warps (thread = key row, two warps per lane quarter split the q columns):
+//     P^T = exp2(S^T scale log2e - LSE log2e), dS^T = P^T (dP^T - Dvec) -> bf16, smem
+//   dV += P^T dO     (M=128 keys, N=64, K=128 q; dO read MN-major)
+//   dK += dS^T Q     (M=128 keys, N=64, K=128 q; Q read MN-major)
+//   dQ  = dS K       (M=128 q, N=64, K=128 keys; dS^T read MN-major as A, K MN-major)
+//   the softmax warps drain dQ (thread = query row) with vector fp32 reductions into
+//   the caller's zeroed accumulator, and finally write dK (scaled) and dV.
+namespace fb {
+constexpr int kM = 128, kD = 64;
+constexpr int kThreads = 384;  // warps 0 (TMA), 1 (MMA), 4..11 (softmax / drain)
+constexpr int kWarpsSm = 8;
+constexpr int kTile = kM * kD * 2;      // 16 KB
+constexpr int kPanel = kM * 128;        // 16 KB: 128 rows x 64 bf16
+// smem: K | V | Q[2] | dO[2] | P^T (2 panels) | dS^T (2 panels) | barriers
+constexpr int kSmemBytes = kTile * 6 + 4 * kPanel + 1024 + 256;
+constexpr uint32_t kTmemCols = 512;  // S 0..127, dP 128..255, dV 256..319, dK 320..383, dQ 384..447
+}  // namespace fb
+
+struct AttnBwdTcParams {
+  int Nq, Nk, d_valid;
+  int n_tiles_k;
+  float scale, scale_log2;
+  int q_pos[4], kv_pos[4];
+  int d1, d2;
+  const float* lse;   // [BH, Nq]
+  const float* dvec;  // [BH, Nq]
+  float* dq;          // fp32 accumulator: (i0, i1, i2, row) strides dq_s0.. dq_row
+  int64_t dq_s0, dq_s1, dq_s2, dq_row;
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  int64_t kv_s0, kv_s1, kv_s2, kv_row;  // dK / dV layout
+  int* status;
+};
+
+__device__ __forceinline__ void red_add_v2(float* addr, float a, float b) {
+  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(addr), "f"(a), "f"(b) : "memory");
+}
+
+__global__ void __launch_bounds__(fb::kThreads, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                       AttnBwdTcParams p) {
+  using namespace fb;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + kTile;
+  uint8_t* sQ = sV + kTile;        // 2 stages
+  uint8_t* sDO = sQ + 2 * kTile;   // 2 stages
+  uint8_t* sP = sDO + 2 * kTile;   // 2 panels
+  uint8_t* sDS = sP + 2 * kPanel;  // 2 panels
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDS + 2 * kPanel);
+  uint64_t* kv_full = bars;        // 1
+  uint64_t* qd_full = bars + 1;    // [2]
+  uint64_t* qd_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 6;
+  uint64_t* p_full = bars + 7;
+  uint64_t* pds_free = bars + 8;
+  uint64_t* dq_full = bars + 9;
+  uint64_t* dq_free = bars + 10;
+  uint64_t* acc_full = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t bh = blockIdx.x / p.n_tiles_k;
+  const int k0 = static_cast<int>(blockIdx.x % p.n_tiles_k) * kM;
+  const int i2 = static_cast<int>(bh % p.d2);
+  const int i1 = static_cast<int>((bh / p.d2) % p.d1);
+  const int i0 = static_cast<int>(bh / (static_cast<int64_t>(p.d1) * p.d2));
+  const int n_qt = (p.Nq + kM - 1) / kM;
+  if (p.status != nullptr && *reinterpret_cast<volatile int*>(p.status) != 0) return;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, kWarpsSm);
+    mbar_init(p_full, kWarpsSm);
+    mbar_init(pds_free, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, kWarpsSm);
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmDO);
+      int c[5];
+      coords_for(p.kv_pos, k0, i2, i1, i0, c);
+      mbar_arrive_expect_tx(kv_full, 2 * kTile);
+      tma_load_5d(sK, &tmK, kv_full, c);
+      tma_load_5d(sV, &tmV, kv_full, c);
+      for (int j = 0; j < n_qt; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&qd_empty[s], ((j >> 1) & 1) ^ 1, p.status, kTimeoutProducer, abort_flag)) break;
+        coords_for(p.q_pos, j * kM, i2, i1, i0, c);
+        mbar_arrive_expect_tx(&qd_full[s], 2 * kTile);
+        tma_load_5d(sQ + s * kTile, &tmQ, &qd_full[s], c);
+        tma_load_5d(sDO + s * kTile, &tmDO, &qd_full[s], c);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t id_s = umma_idesc_bf16(kM, kM, false, false);    // S^T, dP^T
+      constexpr uint32_t id_kv = umma_idesc_bf16(kM, kD, false, true);    // dV, dK: A K-major, B MN-major
+      constexpr uint32_t id_q = umma_idesc_bf16(kM, kD, true, true);      // dQ: A (dS) MN-major, B (K) MN-major
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP), aDS = smem_u32(sDS);
+      bool ok = mbar_wait(kv_full, 0, p.status, kTimeoutMma, abort_flag);
+      for (int j = 0; ok && j < n_qt; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&qd_full[s], (j >> 1) & 1, p.status, kTimeoutMma, abort_flag)) break;
+        if (j >= 1 && !mbar_wait(s_free, (j - 1) & 1, p.status, kTimeoutMma, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t aQ = smem_u32(sQ + s * kTile), aDO = smem_u32(sDO + s * kTile);
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k) {
+          umma_bf16_ss(tS, umma_desc_kmajor_sw128(aK + k * 32), umma_desc_kmajor_sw128(aQ + k * 32), id_s, k > 0);
+          umma_bf16_ss(tDP, umma_desc_kmajor_sw128(aV + k * 32), umma_desc_kmajor_sw128(aDO + k * 32), id_s, k > 0);
+        }
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, j & 1, p.status, kTimeoutMma, abort_flag)) break;
+        if (j >= 1 && !mbar_wait(dq_free, (j - 1) & 1, p.status, kTimeoutMma, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kM / 16; ++k) {
+          // K-major A over q: panel (k >> 2), 32-byte steps; MN-major B over q rows: 2048-byte steps
+          const uint64_t dP = umma_desc_kmajor_sw128(aP + (k >> 2) * kPanel + (k & 3) * 32);
+          const uint64_t dS = umma_desc_kmajor_sw128(aDS + (k >> 2) * kPanel + (k & 3) * 32);
+          umma_bf16_ss(tDV, dP, umma_smem_desc(aDO + k * 2048, 8192, 1024, 2), id_kv, (j > 0 || k > 0));
+          umma_bf16_ss(tDK, dS, umma_smem_desc(aQ + k * 2048, 8192, 1024, 2), id_kv, (j > 0 || k > 0));
+        }
+#pragma unroll
+        for (int k = 0; k < kM / 16; ++k) {
+          // A = dS [q x keys] read MN-major from dS^T (rows = keys): 16 key rows per step
+          const uint64_t da = umma_smem_desc(aDS + k * 2048, kPanel, 1024, 2);
+          const uint64_t db = umma_smem_desc(aK + k * 2048, 8192, 1024, 2);
+          umma_bf16_ss(tDQ, da, db, id_q, k > 0);
+        }
+        umma_commit(pds_free);
+        umma_commit(dq_full);
+        umma_commit(&qd_empty[s]);
+      }
+      if (ok) umma_commit(acc_full);
+    }
+  } else if (warp >= 4) {
+    const int q4 = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const int r = q4 * 32 + lane;  // TMEM lane: key row for S/dP/dK/dV, query row for dQ
+    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    const int key = k0 + r;
+    const bool key_ok = key < p.Nk;
+    constexpr float kLog2e = 1.4426950408889634f;
+    const float* lse_b = p.lse + bh * p.Nq;
+    const float* dv_b = p.dvec + bh * p.Nq;
+    float* dq_b = p.dq + static_cast<int64_t>(i0) * p.dq_s0 + static_cast<int64_t>(i1) * p.dq_s1 +
+                  static_cast<int64_t>(i2) * p.dq_s2;
+    bool ok = true;
+    auto drain_dq = [&](int jj) -> bool {
+      if (!mbar_wait_warp(dq_full, jj & 1, p.status, kTimeoutEpilogue, abort_flag)) return false;
+      tc_fence_after();
+      uint32_t v[32];
+      tmem_ld32(tDQ + lane_off + half * 32, v);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      const int qrow = jj * kM + r;
+      if (qrow < p.Nq) {
+        float* dst = dq_b + static_cast<int64_t>(qrow) * p.dq_row + half * 32;
+#pragma unroll
+        for (int i = 0; i < 32; i += 2)
+          if (half * 32 + i < p.d_valid) red_add_v2(dst + i, __uint_as_float(v[i]) * p.scale, __uint_as_float(v[i + 1]) * p.scale);
+      }
+      return true;
+    };
+    for (int j = 0; ok && j < n_qt; ++j) {
+      if (!mbar_wait_warp(s_full, j & 1, p.status, kTimeoutEpilogue, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[64], dp[64];
+      tmem_ld32(tS + lane_off + half * 64, *reinterpret_cast<uint32_t(*)[32]>(sv));
+      tmem_ld32(tS + lane_off + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+      tmem_ld32(tDP + lane_off + half * 64, *reinterpret_cast<uint32_t(*)[32]>(dp));
+      tmem_ld32(tDP + lane_off + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dp + 32));
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
+      // P and dS of the previous block must have been consumed before we overwrite them
+      if (j >= 1 && !mbar_wait_warp(pds_free, (j - 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const int qbase = j * kM + half * 64;
+      uint8_t* panelP = sP + half * kPanel;
+      uint8_t* panelS = sDS + half * kPanel;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t pk[4], dk4[4];
+#pragma unroll
+        for (int i2p = 0; i2p < 4; ++i2p) {
+          float pe[2], de[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int col = ch * 8 + i2p * 2 + e;
+            const int qi = qbase + col;
+            float pv = 0.f, ds = 0.f;
+            if (key_ok && qi < p.Nq) {
+              pv = exp2_mufu(__uint_as_float(sv[col]) * p.scale_log2 - lse_b[qi] * kLog2e);
+              ds = pv * (__uint_as_float(dp[col]) - dv_b[qi]);
+            }
+            pe[e] = pv;
+            de[e] = ds;
+          }
+          pk[i2p] = pack_bf16x2(pe[0], pe[1]);
+          dk4[i2p] = pack_bf16x2(de[0], de[1]);
+        }
+        *reinterpret_cast<uint4*>(panelP + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(panelS + r * 128 + ((ch ^ (r & 7)) << 4)) =
+            make_uint4(dk4[0], dk4[1], dk4[2], dk4[3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      if (j >= 1 && !drain_dq(j - 1)) {
+        ok = false;
+        break;
+      }
+    }
+    if (ok && n_qt > 0) ok = drain_dq(n_qt - 1);
+    if (ok) ok = mbar_wait_warp(acc_full, 0, p.status, kTimeoutEpilogue, abort_flag);
+    if (ok) {
+      tc_fence_after();
+      uint32_t v[32], w[32];
+      tmem_ld32(tDK + lane_off + half * 32, v);
+      tmem_ld32(tDV + lane_off + half * 32, w);
+      tmem_wait_ld();
+      if (key_ok) {
+        const int64_t off = static_cast<int64_t>(i0) * p.kv_s0 + static_cast<int64_t>(i1) * p.kv_s1 +
+                            static_cast<int64_t>(i2) * p.kv_s2 + static_cast<int64_t>(key) * p.kv_row + half * 32;
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          if (half * 32 + c8 * 8 >= p.d_valid) continue;
+          uint4 a, b;
+          a.x = pack_bf16x2(__uint_as_float(v[c8 * 8]) * p.scale, __uint_as_float(v[c8 * 8 + 1]) * p.scale);
+          a.y = pack_bf16x2(__uint_as_float(v[c8 * 8 + 2]) * p.scale, __uint_as_float(v[c8 * 8 + 3]) * p.scale);
+          a.z = pack_bf16x2(__uint_as_float(v[c8 * 8 + 4]) * p.scale, __uint_as_float(v[c8 * 8 + 5]) * p.scale);
+          a.w = pack_bf16x2(__uint_as_float(v[c8 * 8 + 6]) * p.scale, __uint_as_float(v[c8 * 8 + 7]) * p.scale);
+          b.x = pack_bf16x2(__uint_as_float(w[c8 * 8]), __uint_as_float(w[c8 * 8 + 1]));
+          b.y = pack_bf16x2(__uint_as_float(w[c8 * 8 + 2]), __uint_as_float(w[c8 * 8 + 3]));
+          b.z = pack_bf16x2(__uint_as_float(w[c8 * 8 + 4]), __uint_as_float(w[c8 * 8 + 5]));
+          b.w = pack_bf16x2(__uint_as_float(w[c8 * 8 + 6]), __uint_as_float(w[c8 * 8 + 7]));
+          *reinterpret_cast<uint4*>(p.dk + off + c8 * 8) = a;
+          *reinterpret_cast<uint4*>(p.dv + off + c8 * 8) = b;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ host
 namespace {
 
@@ -435,6 +725,68 @@ void attn_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
   TORCH_CHECK(BH * p.n_tiles_q < 2147483647LL, "attention grid too large");
   dim3 grid(static_cast<unsigned>(BH * p.n_tiles_q));
   attn_fwd_tc_kernel<<<grid, fa::kThreads, fa::kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(mq.map, mk.map, mv.map, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// dK / dV share one layout (ldkv); dq is a zeroed fp32 accumulator addressed through ldq
+// (same head decomposition; 8-byte aligned rows)
+void attn_bwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& dout,
+                 const torch::Tensor& lse, const torch::Tensor& dvec, torch::Tensor& dq, torch::Tensor& dk,
+                 torch::Tensor& dv, std::vector<int64_t> lq, std::vector<int64_t> lkv, std::vector<int64_t> ldo,
+                 std::vector<int64_t> ldkv, std::vector<int64_t> ldq, int64_t BH, int64_t Nq, int64_t Nk,
+                 int64_t d_valid, double scale, const torch::Tensor& status) {
+  for (const torch::Tensor* t : std::initializer_list<const torch::Tensor*>{&q, &k, &v, &dout, &dk, &dv})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16, "attn_bwd_tc: bf16 CUDA tensors");
+  TORCH_CHECK(dq.is_cuda() && dq.scalar_type() == at::kFloat, "attn_bwd_tc: dq must be a zeroed fp32 accumulator");
+  for (int i = 0; i < 4; ++i) TORCH_CHECK(ldq[i] % 2 == 0, "attn_bwd_tc: dq rows must be 8-byte aligned");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && dvec.scalar_type() == at::kFloat, "attn_bwd_tc: fp32 lse / dvec");
+  TORCH_CHECK(d_valid > 0 && d_valid <= 64 && d_valid % 8 == 0, "attn_bwd_tc: head dim multiple of 8, <= 64");
+  TORCH_CHECK(lq[4] == lkv[4] && lq[5] == lkv[5] && lq[4] == ldo[4] && lq[5] == ldo[5] && lq[4] == ldkv[4] &&
+                  lq[5] == ldkv[5],
+              "attn_bwd_tc: shared head decomposition");
+  for (int i = 0; i < 4; ++i) TORCH_CHECK(ldkv[i] % 8 == 0, "attn_bwd_tc: dK / dV rows must be 16-byte aligned");
+  const at::cuda::CUDAGuard guard(q.device());
+  if (BH == 0 || Nq == 0 || Nk == 0) return;
+  const int64_t n_i0 = BH / (lq[4] * lq[5]);
+  Map5 mq = make_map(q, lq, Nq, n_i0, static_cast<int>(d_valid));
+  Map5 mdo = make_map(dout, ldo, Nq, n_i0, static_cast<int>(d_valid));
+  Map5 mk = make_map(k, lkv, Nk, n_i0, static_cast<int>(d_valid));
+  Map5 mv = make_map(v, lkv, Nk, n_i0, static_cast<int>(d_valid));
+  TORCH_CHECK(std::equal(mq.pos, mq.pos + 4, mdo.pos), "attn_bwd_tc: Q and dO layouts must sort alike");
+  AttnBwdTcParams p{};
+  p.Nq = static_cast<int>(Nq);
+  p.Nk = static_cast<int>(Nk);
+  p.d_valid = static_cast<int>(d_valid);
+  p.scale = static_cast<float>(scale);
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  std::copy(mq.pos, mq.pos + 4, p.q_pos);
+  std::copy(mk.pos, mk.pos + 4, p.kv_pos);
+  p.d1 = static_cast<int>(lq[4]);
+  p.d2 = static_cast<int>(lq[5]);
+  p.lse = lse.data_ptr<float>();
+  p.dvec = dvec.data_ptr<float>();
+  p.dq = dq.data_ptr<float>();
+  p.dq_s0 = ldq[0];
+  p.dq_s1 = ldq[1];
+  p.dq_s2 = ldq[2];
+  p.dq_row = ldq[3];
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  p.kv_s0 = ldkv[0];
+  p.kv_s1 = ldkv[1];
+  p.kv_s2 = ldkv[2];
+  p.kv_row = ldkv[3];
+  p.status = status.defined() && status.numel() > 0 ? status.data_ptr<int>() : nullptr;
+  p.n_tiles_k = static_cast<int>((Nk + fb::kM - 1) / fb::kM);
+  static bool configured[64] = {false};
+  const int dev = q.get_device();
+  if (!configured[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fb::kSmemBytes));
+    configured[dev] = true;
+  }
+  TORCH_CHECK(BH * p.n_tiles_k < 2147483647LL, "attention grid too large");
+  attn_bwd_tc_kernel<<<static_cast<unsigned>(BH * p.n_tiles_k), fb::kThreads, fb::kSmemBytes,
+                       at::cuda::getCurrentCUDAStream()>>>(mq.map, mk.map, mv.map, mdo.map, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

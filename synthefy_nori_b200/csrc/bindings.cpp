@@ -56,6 +56,13 @@ void peer_ipc_close(int64_t ptr);
 torch::Tensor tensor_from_ptr(int64_t ptr, int64_t numel, int64_t device, c10::ScalarType dtype);
 std::vector<torch::Tensor> quantile_decode(const torch::Tensor& pred, const torch::Tensor& taus,
                                            const torch::Tensor& levels, bool return_sorted);
+void attn_bwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& dout,
+                 const torch::Tensor& lse, const torch::Tensor& dvec, torch::Tensor& dq, torch::Tensor& dk,
+                 torch::Tensor& dv, std::vector<int64_t> lq, std::vector<int64_t> lkv, std::vector<int64_t> ldo,
+                 std::vector<int64_t> ldkv, std::vector<int64_t> ldq, int64_t BH, int64_t Nq, int64_t Nk,
+                 int64_t d_valid, double scale, const torch::Tensor& status);
+torch::Tensor attn_dvec(const torch::Tensor& o, const torch::Tensor& dout, std::vector<int64_t> lo,
+                        std::vector<int64_t> ldo, int64_t BH, int64_t Nq, int64_t d_valid);
 torch::Tensor rms_scale(const torch::Tensor& x, double eps);
 torch::Tensor sumsq_to_scale(const torch::Tensor& ssq, int64_t E, double eps);
 std::vector<torch::Tensor> pinball_fused(const torch::Tensor& pred, const torch::Tensor& target,
@@ -79,6 +86,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &nori::attn_bwd);
   m.def("attn_fwd_tc", &nori::attn_fwd_tc);
   m.def("attn_fwd_q8", &nori::attn_fwd_q8);
+  m.def("attn_bwd_tc", &nori::attn_bwd_tc);
+  m.def("attn_dvec", &nori::attn_dvec);
   m.def("rms_scale", &nori::rms_scale);
   m.def("quantile_decode", &nori::quantile_decode);
   m.def("peer_ddp_step", &nori::peer_ddp_step);

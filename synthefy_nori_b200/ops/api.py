@@ -18,6 +18,7 @@ __all__ = [
     "attention_bwd",
     "attention_fwd_tc",
     "attention_fwd_q8",
+    "attention_bwd_tc",
     "rms_scale",
     "rms_apply",
     "rms_bwd",
@@ -117,6 +118,14 @@ def attention_fwd_q8(q, kv, scales, o, *, lq, lkv, lscale, lo, BH, Nq, Nk, d, sc
     _lib().attn_fwd_q8(q, kv, scales, o, lse, _layout(lq), _layout(lkv), _layout(lscale), _layout(lo), int(E), int(H),
                        int(BH), int(Nq), int(Nk), int(d), float(scale))
     return o
+
+
+def attention_bwd_tc(q, k, v, o, do, lse, dq_f32, dk, dv, *, lq, lkv, lo, ldo, ldkv, ldq, BH, Nq, Nk, d, scale):
+    """tcgen05 / TMEM flash-attention backward (128-key CTAs, 128-query blocks). dK and dV
+    share ``ldkv``; ``dq_f32`` is a zeroed fp32 accumulator addressed through ``ldq``."""
+    dvec = _lib().attn_dvec(o, do, _layout(lo), _layout(ldo), int(BH), int(Nq), int(d))
+    _lib().attn_bwd_tc(q, k, v, do, lse, dvec, dq_f32, dk, dv, _layout(lq), _layout(lkv), _layout(ldo), _layout(ldkv),
+                       _layout(ldq), int(BH), int(Nq), int(Nk), int(d), float(scale), status_word(q.device))
 
 
 def attention_bwd(q, k, v, o, do, lse, dq_f32, dk, dv, *, lq, lk, lv, lo, ldo, ldk, ldv, BH, Nq, Nk, d, scale,
