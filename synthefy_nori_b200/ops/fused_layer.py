@@ -222,9 +222,9 @@ class SeqSublayer(torch.autograd.Function):
         dy_ctx = torch.empty(g.R_ctx, 5 * E, device=dev, dtype=BF16)
         lc, l5 = _seq_layout(g.ep, g, E), _seq_layout(g.ep, g, 5 * E)
         dq_self = torch.zeros(g.R_ctx, E, device=dev, dtype=torch.float32)
-        ops.attention_bwd(q_self, y_ctx[:, E : 2 * E], y_ctx[:, 2 * E : 3 * E], o_ctx, do_ctx, lse_ctx, dq_self,
-                          dy_ctx[:, E : 2 * E], dy_ctx[:, 2 * E : 3 * E], lq=lc, lk=l5, lv=l5, lo=lc, ldo=lc, ldk=l5,
-                          ldv=l5, ldq=lc, BH=BTH, Nq=g.ep, Nk=g.ep, d=D, scale=scale)
+        ops.attention_bwd_tc(q_self, y_ctx[:, E : 2 * E], y_ctx[:, 2 * E : 3 * E], o_ctx, do_ctx, lse_ctx, dq_self,
+                             dy_ctx[:, E : 2 * E], dy_ctx[:, 2 * E : 3 * E], lq=lc, lkv=l5, lo=lc, ldo=lc, ldkv=l5,
+                             ldq=lc, BH=BTH, Nq=g.ep, Nk=g.ep, d=D, scale=scale)
         qp_self, qp_cross = list(qparams[:8]), list(qparams[8:])
         grads_qp = [None] * len(qparams)
         if qmode:
@@ -239,9 +239,9 @@ class SeqSublayer(torch.autograd.Function):
             ops.gemm_wgrad(o_q, d_q, dwo_cross, alpha=alpha)
             lq = _seq_layout(g.nq, g, E)
             dq_c = torch.zeros(g.R_q, E, device=dev, dtype=torch.float32)
-            ops.attention_bwd(q_cross, y_ctx[:, 3 * E : 4 * E], y_ctx[:, 4 * E :], o_q, do_q, lse_q, dq_c,
-                              dy_ctx[:, 3 * E : 4 * E], dy_ctx[:, 4 * E :], lq=lq, lk=l5, lv=l5, lo=lq, ldo=lq,
-                              ldk=l5, ldv=l5, ldq=lq, BH=BTH, Nq=g.nq, Nk=g.ep, d=D, scale=scale)
+            ops.attention_bwd_tc(q_cross, y_ctx[:, 3 * E : 4 * E], y_ctx[:, 4 * E :], o_q, do_q, lse_q, dq_c,
+                                 dy_ctx[:, 3 * E : 4 * E], dy_ctx[:, 4 * E :], lq=lq, lkv=l5, lo=lq, ldo=lq, ldkv=l5,
+                                 ldq=lq, BH=BTH, Nq=g.nq, Nk=g.ep, d=D, scale=scale)
             if qmode:
                 dy_q, gq = _qass_backward(qp_cross, qmode, y_q, g.ep, g, dq_c)
                 grads_qp[8:] = gq

@@ -71,6 +71,17 @@ def bench_attn(a):
         fn = lambda: ops.attention_fwd_tc(q, k, v, o, lse=lse, **kw)  # noqa: E731
     elif a.kernel == "mma":
         fn = lambda: ops.attention_fwd(q, k, v, o, lse=lse, **kw)  # noqa: E731
+    elif a.kernel == "bwdtc":
+        ops.attention_fwd_tc(q, k, v, o, lse=lse, **kw)
+        do = torch.randn_like(q)
+        dq = torch.zeros(BH, N, D, device="cuda")
+        dk, dv = torch.empty_like(q), torch.empty_like(q)
+        flops *= 2.5
+
+        def fn():
+            dq.zero_()
+            ops.attention_bwd_tc(q, k, v, o, do, lse, dq, dk, dv, lq=lay, lkv=lay, lo=lay, ldo=lay, ldkv=lay, ldq=lay,
+                                 BH=BH, Nq=N, Nk=N, d=D, scale=1 / math.sqrt(D))
     elif a.kernel == "bwd":
         ops.attention_fwd_tc(q, k, v, o, lse=lse, **kw)
         do = torch.randn_like(q)
