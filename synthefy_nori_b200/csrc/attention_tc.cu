@@ -35,7 +35,7 @@ constexpr int kM = 128;      // query rows per CTA
 constexpr int kN = 128;      // keys per tile
 constexpr int kD = 64;       // padded head dim
 constexpr int kThreads = 384;  // warps 0 (TMA), 1 (MMA), 4..11 (softmax)
-constexpr int kSoftmaxThreads = 256;
+
 constexpr int kSoftmaxWarps = 8;  // softmax-side barriers take one arrive per warp
 constexpr int kTileBytes = kM * kD * 2;  // 16 KB (Q, K or V tile)
 constexpr int kPBytes = kM * kN * 2;     // 32 KB (P tile: two 64-key panels)
@@ -413,6 +413,8 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
   uint64_t* acc_full = bars + 11;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // per-stage query vectors: LSE (log2 units) and Dvec of the block's 128 queries
+  __shared__ float s_lse[2][kM], s_dv[2][kM];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int64_t bh = blockIdx.x / p.n_tiles_k;
@@ -426,7 +428,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_full[i], 2);  // TMA (expect_tx) + the producer warp's vector loads
       mbar_init(&qd_empty[i], 1);
     }
     mbar_init(s_full, 1);
@@ -447,7 +449,11 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
   const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
 
   if (warp == 0) {
-    if (elect_one()) {
+    // whole warp: lane 0 issues the TMA loads, all lanes stage LSE / Dvec of the block
+    const float* lse_g = p.lse + bh * p.Nq;
+    const float* dv_g = p.dvec + bh * p.Nq;
+    constexpr float kLog2e = 1.4426950408889634f;
+    if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
@@ -457,14 +463,24 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       mbar_arrive_expect_tx(kv_full, 2 * kTile);
       tma_load_5d(sK, &tmK, kv_full, c);
       tma_load_5d(sV, &tmV, kv_full, c);
-      for (int j = 0; j < n_qt; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&qd_empty[s], ((j >> 1) & 1) ^ 1, p.status, kTimeoutProducer, abort_flag)) break;
+    }
+    for (int j = 0; j < n_qt; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait_warp(&qd_empty[s], ((j >> 1) & 1) ^ 1, p.status, kTimeoutProducer, abort_flag)) break;
+      if (lane == 0) {
+        int c[5];
         coords_for(p.q_pos, j * kM, i2, i1, i0, c);
         mbar_arrive_expect_tx(&qd_full[s], 2 * kTile);
         tma_load_5d(sQ + s * kTile, &tmQ, &qd_full[s], c);
         tma_load_5d(sDO + s * kTile, &tmDO, &qd_full[s], c);
       }
+      for (int i = lane; i < kM; i += 32) {
+        const int qi = j * kM + i;
+        s_lse[s][i] = qi < p.Nq ? lse_g[qi] * kLog2e : INFINITY;
+        s_dv[s][i] = qi < p.Nq ? dv_g[qi] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&qd_full[s]);
     }
   } else if (warp == 1) {
     if (elect_one()) {
@@ -516,9 +532,6 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
     const int key = k0 + r;
     const bool key_ok = key < p.Nk;
-    constexpr float kLog2e = 1.4426950408889634f;
-    const float* lse_b = p.lse + bh * p.Nq;
-    const float* dv_b = p.dvec + bh * p.Nq;
     float* dq_b = p.dq + static_cast<int64_t>(i0) * p.dq_s0 + static_cast<int64_t>(i1) * p.dq_s1 +
                   static_cast<int64_t>(i2) * p.dq_s2;
     bool ok = true;
@@ -545,7 +558,14 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         ok = false;
         break;
       }
+      // the block's LSE / Dvec were staged before qd_full completed (acquire it here too)
+      if (!mbar_wait_warp(&qd_full[j & 1], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
+      const float* sl = s_lse[j & 1] + half * 64;
+      const float* sd = s_dv[j & 1] + half * 64;
       uint32_t sv[64], dp[64];
       tmem_ld32(tS + lane_off + half * 64, *reinterpret_cast<uint32_t(*)[32]>(sv));
       tmem_ld32(tS + lane_off + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
@@ -575,8 +595,8 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
             const int qi = qbase + col;
             float pv = 0.f, ds = 0.f;
             if (key_ok && qi < p.Nq) {
-              pv = exp2_mufu(__uint_as_float(sv[col]) * p.scale_log2 - lse_b[qi] * kLog2e);
-              ds = pv * (__uint_as_float(dp[col]) - dv_b[qi]);
+              pv = exp2_mufu(fmaf(__uint_as_float(sv[col]), p.scale_log2, -sl[col]));
+              ds = pv * (__uint_as_float(dp[col]) - sd[col]);
             }
             pe[e] = pv;
             de[e] = ds;
