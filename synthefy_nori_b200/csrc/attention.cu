@@ -713,6 +713,140 @@ void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
 }  // namespace nori
 
 namespace nori {
+// ---------------------------------------------------------------- multi-shard int8 K/V forward
+// Context-row-sharded inference: the keys of one table are split over up to 8 ranks and
+// each rank's int8 K/V shard lives in its own (IPC-shared) memory. One query CTA walks the
+// tiles of every shard in turn - peer shards are read over NVLink with plain loads and
+// dequantised on the way into shared memory - so the online softmax (running max and sum)
+// spans the whole context and the result needs no separate partial-softmax merge.
+constexpr int kMaxShards = 8;
+struct AttnShardsParams {
+  const __nv_bfloat16* q;
+  __nv_bfloat16* o;
+  float* lse;
+  const int8_t* kv[kMaxShards];     // shard base (K columns; V at +E)
+  const float* sc[kMaxShards];      // shard scale base (K heads; V heads at +H)
+  int nk[kMaxShards];               // keys per shard
+  int64_t kv_s0[kMaxShards];        // per-shard table stride (elements)
+  int64_t sc_s0[kMaxShards];
+  Layout3 lq, lkv, ls, lo;          // lkv / ls: s1, s2, row strides shared by all shards
+  int n_shards, E, H;
+  int BH, Nq, d_valid, n_tiles_q;
+  float scale_log2;
+};
+
+__global__ void __launch_bounds__(kAttnThreads) attn_fwd_q8_shards_kernel(AttnShardsParams p) {
+  __shared__ __align__(128) uint8_t sq[kBlkQ * 128];
+  __shared__ __align__(128) uint8_t sk[kBlkK * 128];
+  __shared__ __align__(128) uint8_t sv[kBlkK * 128];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t bh = blockIdx.x / p.n_tiles_q;
+  const int q0 = static_cast<int>(blockIdx.x % p.n_tiles_q) * kBlkQ;
+  load_tile(sq, p.q + p.lq.offset(bh, 0), p.lq.row, q0, p.Nq, p.d_valid, tid, kAttnThreads);
+  cp_async_commit();
+  cp_async_wait<0>();
+  // head decomposition for the per-shard offsets (table index i0 uses the shard's own stride)
+  const int64_t i2 = bh % p.lkv.d2;
+  const int64_t t = bh / p.lkv.d2;
+  const int64_t i1 = t % p.lkv.d1;
+  const int64_t i0 = t / p.lkv.d1;
+  FwdState st;
+  bool init = false;
+  for (int sh = 0; sh < p.n_shards; ++sh) {
+    const int nk = p.nk[sh];
+    const int8_t* kb = p.kv[sh] + i0 * p.kv_s0[sh] + i1 * p.lkv.s1 + i2 * p.lkv.s2;
+    const float* ksb = p.sc[sh] + i0 * p.sc_s0[sh] + i1 * p.ls.s1 + i2 * p.ls.s2;
+    const int n_tiles = (nk + kBlkK - 1) / kBlkK;
+    for (int tt = 0; tt < n_tiles; ++tt) {
+      load_tile_q8(sk, kb, ksb, p.lkv.row, p.ls.row, tt * kBlkK, nk, p.d_valid, tid, kAttnThreads);
+      load_tile_q8(sv, kb + p.E, ksb + p.H, p.lkv.row, p.ls.row, tt * kBlkK, nk, p.d_valid, tid, kAttnThreads);
+      __syncthreads();
+      if (!init) {
+        fwd_init(st, sq, warp, lane);
+        init = true;
+      }
+      fwd_tile(st, sk, sv, tt * kBlkK, nk, p.scale_log2, lane);
+      __syncthreads();
+    }
+  }
+  if (init) fwd_store(st, p.o + p.lo.offset(bh, 0), p.lo.row, p.lse, bh, q0, p.Nq, p.d_valid, warp, lane);
+}
+
+void attn_fwd_q8_shards(const torch::Tensor& q, std::vector<int64_t> kv_ptrs, std::vector<int64_t> sc_ptrs,
+                        std::vector<int64_t> nks, std::vector<int64_t> kv_s0, std::vector<int64_t> sc_s0,
+                        torch::Tensor& o, const c10::optional<torch::Tensor>& lse, std::vector<int64_t> lq,
+                        std::vector<int64_t> lkv, std::vector<int64_t> ls, std::vector<int64_t> lo, int64_t E,
+                        int64_t H, int64_t BH, int64_t Nq, int64_t d_valid, double scale) {
+  check_bf16(q, "q");
+  check_bf16(o, "o");
+  const size_t ns = kv_ptrs.size();
+  TORCH_CHECK(ns >= 1 && ns <= static_cast<size_t>(kMaxShards) && sc_ptrs.size() == ns && nks.size() == ns &&
+                  kv_s0.size() == ns && sc_s0.size() == ns,
+              "attn_fwd_q8_shards: 1..8 shards with one pointer / size / stride each");
+  TORCH_CHECK(d_valid > 0 && d_valid <= kD && d_valid % 8 == 0, "attn_fwd_q8_shards: head dim multiple of 8, <= 64");
+  const at::cuda::CUDAGuard guard(q.device());
+  if (BH == 0 || Nq == 0) return;
+  AttnShardsParams p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.n_shards = static_cast<int>(ns);
+  int64_t total = 0;
+  for (size_t i = 0; i < ns; ++i) {
+    TORCH_CHECK(kv_ptrs[i] % 8 == 0 && sc_ptrs[i] % 4 == 0, "attn_fwd_q8_shards: misaligned shard base");
+    p.kv[i] = reinterpret_cast<const int8_t*>(kv_ptrs[i]);
+    p.sc[i] = reinterpret_cast<const float*>(sc_ptrs[i]);
+    p.nk[i] = static_cast<int>(nks[i]);
+    p.kv_s0[i] = kv_s0[i];
+    p.sc_s0[i] = sc_s0[i];
+    total += nks[i];
+  }
+  TORCH_CHECK(total > 0, "attn_fwd_q8_shards: at least one key");
+  p.lq = to_layout(lq);
+  p.lkv = to_layout(lkv);
+  p.ls = to_layout(ls);
+  p.lo = to_layout(lo);
+  TORCH_CHECK(p.lkv.row % 8 == 0 && p.lkv.s1 % 8 == 0 && p.lkv.s2 % 8 == 0, "attn_fwd_q8_shards: 8-byte K/V rows");
+  p.E = static_cast<int>(E);
+  p.H = static_cast<int>(H);
+  p.BH = static_cast<int>(BH);
+  p.Nq = static_cast<int>(Nq);
+  p.d_valid = static_cast<int>(d_valid);
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  if (lse.has_value() && lse->defined()) p.lse = lse->data_ptr<float>();
+  p.n_tiles_q = static_cast<int>((Nq + kBlkQ - 1) / kBlkQ);
+  attn_fwd_q8_shards_kernel<<<static_cast<unsigned>(BH * p.n_tiles_q), kAttnThreads, 0,
+                              at::cuda::getCurrentCUDAStream()>>>(p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Plain-load copy of a row-strided 2-D region (e.g. a peer's K/V columns) into local memory.
+__global__ void copy_rows_kernel(const uint8_t* __restrict__ src, int64_t src_ld, uint8_t* __restrict__ dst,
+                                 int64_t dst_ld, int64_t rows, int64_t row_bytes) {
+  const int64_t chunks = row_bytes / 16;
+  const int64_t total = rows * chunks;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / chunks, c = i % chunks;
+    *reinterpret_cast<uint4*>(dst + r * dst_ld + c * 16) = *reinterpret_cast<const uint4*>(src + r * src_ld + c * 16);
+  }
+}
+
+void copy_rows(int64_t src_ptr, int64_t src_ld_bytes, torch::Tensor& dst, int64_t dst_ld_bytes, int64_t rows,
+               int64_t row_bytes) {
+  TORCH_CHECK(dst.is_cuda(), "copy_rows: CUDA destination");
+  TORCH_CHECK(src_ptr % 16 == 0 && reinterpret_cast<uintptr_t>(dst.data_ptr()) % 16 == 0 && src_ld_bytes % 16 == 0 &&
+                  dst_ld_bytes % 16 == 0 && row_bytes % 16 == 0,
+              "copy_rows: 16-byte aligned rows");
+  const at::cuda::CUDAGuard guard(dst.device());
+  if (rows == 0 || row_bytes == 0) return;
+  const int64_t total = rows * (row_bytes / 16);
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 8));
+  copy_rows_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const uint8_t*>(src_ptr), src_ld_bytes, reinterpret_cast<uint8_t*>(dst.data_ptr()),
+      dst_ld_bytes, rows, row_bytes);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // Dvec = rowsum(dO * O) for the tensor-core backward (same kernel as attn_bwd's first step).
 torch::Tensor attn_dvec(const torch::Tensor& o, const torch::Tensor& dout, std::vector<int64_t> lo,
                         std::vector<int64_t> ldo, int64_t BH, int64_t Nq, int64_t d_valid) {

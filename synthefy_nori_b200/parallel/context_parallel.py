@@ -1,0 +1,209 @@
+"""Context-row-sharded inference over NVLink peer memory.
+
+One table's context rows are split over the ranks of one node. Every rank embeds the
+whole context (the embedding is cheap and the column statistics must be global), then
+runs the encoder stack on its own row shard only:
+
+* context self-attention (per layer): each rank projects Q/K/V for its rows into an
+  IPC-shared staging buffer; after a barrier every rank copies the peers' K/V rows into
+  local memory with a plain-load P2P copy kernel (no TMA from peer memory) and runs the
+  tcgen05 attention for its queries against all keys;
+* the cross-attention K/V that query rows will use is quantised to int8 (per token and
+  head, the reference's absmax rule) into an IPC-shared per-layer cache shard;
+* query rows (split over ranks) run the cached stack; their cross-attention kernel walks
+  the int8 K/V tiles of every rank's shard - peer shards read over NVLink with plain
+  loads and dequantised while staged - so the online softmax covers the whole context in
+  one pass (``attn_fwd_q8_shards``).
+
+The reference has no multi-GPU context path: its long-context rungs are single-GPU
+(resident int8, host offload, streamed blocks with an LSE merge, ``model/layer.py:747-934``,
+``inference/memory_policy.py``).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from synthefy_nori_b200 import ops
+from synthefy_nori_b200.ops.fused_layer import (
+    BF16,
+    Geometry,
+    _cached_bf16,
+    _feat_forward,
+    _mlp_forward,
+    _qass_apply,
+    _seq_layout,
+    check_supported,
+    layer_weights,
+)
+from synthefy_nori_b200.parallel.peer_reduce import exchange_handles, shard_bounds
+
+
+class PeerRegion:
+    """One IPC-shareable device allocation per rank, opened by every other rank."""
+
+    def __init__(self, nbytes: int, device: torch.device, group=None):
+        self.C = ops.lib()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.nbytes = int(max(nbytes, 256))
+        self.device = device
+        self.local = self.C.peer_malloc(self.nbytes)
+        h = bytes(self.C.peer_ipc_handle(self.local).numpy().tobytes())
+        allh = exchange_handles({"h": h}, group)
+        self.ptrs, self._opened = [], []
+        for r, d in enumerate(allh):
+            if r == self.rank:
+                self.ptrs.append(self.local)
+            else:
+                p = self.C.peer_ipc_open(torch.frombuffer(bytearray(d["h"]), dtype=torch.uint8))
+                self._opened.append(p)
+                self.ptrs.append(p)
+
+    def view(self, offset: int, numel: int, dtype: torch.dtype) -> torch.Tensor:
+        """Local tensor view of ``numel`` elements at byte ``offset``."""
+        esize = torch.empty((), dtype=dtype).element_size()
+        if offset % 16 or offset + numel * esize > self.nbytes:
+            raise ValueError("PeerRegion.view out of range or misaligned")
+        t = self.C.tensor_from_ptr(self.local + offset, numel * esize, self.device.index, torch.uint8)
+        return t.view(dtype)
+
+    def close(self) -> None:
+        if self.local is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+        for p in self._opened:
+            self.C.peer_ipc_close(p)
+        dist.barrier(self.group)
+        self.C.peer_free(self.local)
+        self.local = None
+
+
+def _align16(n: int) -> int:
+    return (n + 15) // 16 * 16
+
+
+class ShardedContextPredictor:
+    """Build a row-sharded int8 context cache across the ranks of ``group`` and answer
+    queries against it (see module docstring)."""
+
+    def __init__(self, model, device: torch.device, group=None):
+        check_supported(model)
+        self.model = model.to(device).eval()
+        self.device = device
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.layers = list(model.transformer_encoder.layers)
+        self.E, self.H = model.embed_dim, model.nhead
+        self.D = self.E // self.H
+        self.regions: list[PeerRegion] = []
+
+    # ------------------------------------------------------------------ build
+    @torch.no_grad()
+    def build(self, x_ctx: torch.Tensor, y_ctx: torch.Tensor) -> None:
+        """``x_ctx [1, N, F]``, ``y_ctx [1, N]``: the full context, identical on every rank."""
+        if x_ctx.shape[0] != 1:
+            raise ValueError("the sharded context path takes one table")
+        model, E, H, D = self.model, self.E, self.H, self.D
+        tokens, meta = model.context_tokens(x_ctx, y_ctx)
+        N, T = tokens.shape[1], tokens.shape[2]
+        b = shard_bounds(N, self.world, align=1)
+        self.bounds = b
+        self.n_rows = [b[i + 1] - b[i] for i in range(self.world)]
+        off, n_loc = b[self.rank], self.n_rows[self.rank]
+        self.meta, self.N, self.T = meta, N, T
+        x = tokens[:, off : off + n_loc].to(BF16).reshape(-1, E).contiguous()
+        R = x.shape[0]
+        L = len(self.layers)
+        # IPC regions: per-layer projection staging (K/V self read by peers) and the cache shard
+        max_rows = max(self.n_rows) * T
+        self.stage = PeerRegion(max_rows * 5 * E * 2, self.device, self.group)
+        kv_bytes = _align16(R * 2 * E)
+        sc_bytes = _align16(R * 2 * H * 4)
+        self.kv_layer_bytes = kv_bytes + sc_bytes
+        self.cache = PeerRegion(L * self.kv_layer_bytes, self.device, self.group)
+        self.regions = [self.stage, self.cache]
+        self.kv_off, self.sc_off = 0, kv_bytes
+        # every rank's shard layout (rows per rank differ by at most one)
+        self.peer_kv_layer_bytes = []
+        for p in range(self.world):
+            rp = self.n_rows[p] * T
+            self.peer_kv_layer_bytes.append((_align16(rp * 2 * E), _align16(rp * 2 * E) + _align16(rp * 2 * H * 4)))
+        kvfull = torch.empty(N * T, 2 * E, device=self.device, dtype=BF16)
+        g_loc = Geometry(B=1, ep=n_loc, nq=0, T=T, E=E, H=H)
+        for li, layer in enumerate(self.layers):
+            w = layer_weights(layer)
+            wb = _cached_bf16(layer, w)
+            rs = ops.rms_scale(x, layer.layer_norm_eps)
+            y = self.stage.view(0, R * 5 * E, BF16).view(R, 5 * E)
+            ops.gemm(x, wb["w_ctx"], row_scale=rs, out=y)
+            torch.cuda.synchronize(self.device)
+            dist.barrier(self.group)
+            for p in range(self.world):
+                rp = self.n_rows[p] * T
+                ops.lib().copy_rows(self.stage.ptrs[p] + E * 2, 5 * E * 2, kvfull[b[p] * T :], 2 * E * 2, rp, 2 * E * 2)
+            q = _qass_apply(w["qp"][:8], w["qmode"], y[:, :E], N, H, D) if w["qmode"] else y[:, :E].contiguous()
+            o = torch.empty(R, E, device=self.device, dtype=BF16)
+            lq = _seq_layout(n_loc, g_loc, E)
+            lkv = (N * T * 2 * E, 2 * E, D, T * 2 * E, T, H)
+            ops.attention_fwd_tc(q, kvfull[:, :E], kvfull[:, E:], o, lq=lq, lk=lkv, lv=lkv, lo=lq, BH=T * H, Nq=n_loc,
+                                 Nk=N, d=D, scale=1.0 / math.sqrt(D))
+            # int8 cross K/V shard of this layer
+            q8, sc = ops.quantize_int8(y[:, 3 * E :].reshape(R, 2, H, D))
+            base = li * self.kv_layer_bytes
+            self.cache.view(base + self.kv_off, R * 2 * E, torch.int8).copy_(q8.reshape(-1))
+            self.cache.view(base + self.sc_off, R * 2 * H, torch.float32).copy_(sc.reshape(-1))
+            x = ops.gemm_residual(o, wb["wo_self_t"], x, layer.alpha)
+            torch.cuda.synchronize(self.device)
+            dist.barrier(self.group)  # peers finished reading this layer's staging buffer
+            wq = {"wb": wb}
+            x = _mlp_forward(layer, wq, x)
+            x = _feat_forward(layer, wq, x, g_loc)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+
+    # ------------------------------------------------------------------ queries
+    @torch.no_grad()
+    def predict_raw(self, x_q: torch.Tensor) -> torch.Tensor:
+        """Quantile outputs ``[1, Nq, K]`` for this rank's query rows ``x_q [1, Nq, F]``."""
+        model, E, H, D, T = self.model, self.E, self.H, self.D, self.T
+        tok = model.query_tokens(x_q, self.meta)
+        nq = tok.shape[1]
+        x = tok.to(BF16).reshape(-1, E).contiguous()
+        g = Geometry(B=1, ep=self.N, nq=nq, T=T, E=E, H=H)
+        lq = _seq_layout(nq, g, E)
+        lkv = (0, 2 * E, D, T * 2 * E, T, H)
+        ls = (0, 2 * H, 1, T * 2 * H, T, H)
+        for li, layer in enumerate(self.layers):
+            w = layer_weights(layer)
+            wb = _cached_bf16(layer, w)
+            rs = ops.rms_scale(x, layer.layer_norm_eps)
+            yq = ops.gemm(x, wb["w_q"], row_scale=rs)
+            q = _qass_apply(w["qp"][8:], w["qmode"], yq, self.N, H, D) if w["qmode"] else yq
+            o = torch.empty(x.shape[0], E, device=self.device, dtype=BF16)
+            kv_ptrs, sc_ptrs = [], []
+            for p in range(self.world):
+                kvb, _ = self.peer_kv_layer_bytes[p]
+                layer_bytes = self.peer_kv_layer_bytes[p][1]
+                kv_ptrs.append(self.cache.ptrs[p] + li * layer_bytes)
+                sc_ptrs.append(self.cache.ptrs[p] + li * layer_bytes + kvb)
+            ops.lib().attn_fwd_q8_shards(q, kv_ptrs, sc_ptrs, self.n_rows, [0] * self.world, [0] * self.world, o, None,
+                                         list(lq), list(lkv), list(ls), list(lq), E, H, T * H, nq, D,
+                                         1.0 / math.sqrt(D))
+            x = ops.gemm_residual(o, wb["wo_cross_t"], x, layer.alpha)
+            wq = {"wb": wb}
+            x = _mlp_forward(layer, wq, x)
+            x = _feat_forward(layer, wq, x, g)
+        h = x.view(1, nq, T, E)[:, :, -1]
+        return model.decode_regression(model.encoder_out_norm(h.float()))
+
+    def close(self) -> None:
+        for r in self.regions:
+            r.close()
+        self.regions = []
