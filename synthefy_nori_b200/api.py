@@ -66,7 +66,8 @@ class NoriRegressor(RegressorMixin, BaseEstimator):
         device=None,
         weights: str | None = None,
         n_estimators: int = 1,
-        cache_dtype: Literal["bf16", "int8"] = "bf16",
+        cache_dtype: Literal["bf16", "int8"] | None = None,
+        memory_policy=None,
         query_chunk_size: int | None = None,
         quantile_collapse: str = "mean",
         random_state: int = 0,
@@ -77,6 +78,7 @@ class NoriRegressor(RegressorMixin, BaseEstimator):
         self.weights = weights
         self.n_estimators = n_estimators
         self.cache_dtype = cache_dtype
+        self.memory_policy = memory_policy
         self.query_chunk_size = query_chunk_size
         self.quantile_collapse = quantile_collapse
         self.random_state = random_state
@@ -102,10 +104,41 @@ class NoriRegressor(RegressorMixin, BaseEstimator):
         from synthefy_nori_b200.inference.predictor import NoriPredictor
 
         if getattr(self, "predictor_", None) is None:
-            self.predictor_ = NoriPredictor(self._load_model(), self.device_, n_estimators=self.n_estimators,
-                                            cache_dtype=self.cache_dtype, query_chunk_size=self.query_chunk_size,
-                                            seed=self.random_state)
+            model = self._load_model()
+            dtype = self._resolve_memory(model)
+            self.predictor_ = NoriPredictor(model, self.device_, n_estimators=self.n_estimators, cache_dtype=dtype,
+                                            query_chunk_size=self.query_chunk_size, seed=self.random_state)
         return self.predictor_
+
+    def _resolve_memory(self, model) -> str:
+        """Pick the cache rung for this table (reference ``MemoryPolicy.resolve``)."""
+        import math as _math
+
+        from synthefy_nori_b200.inference.degradation import CacheQuantizedWarning, ContextSubsampledWarning
+        from synthefy_nori_b200.inference.memory_policy import MemoryPolicy
+
+        pol = MemoryPolicy.coerce(self.memory_policy)
+        if self.cache_dtype is not None:
+            pol = pol.model_copy(update={"cache_dtype": self.cache_dtype})
+        if self.device_.type == "cuda":
+            total = torch.cuda.get_device_properties(self.device_).total_memory / 1024 ** 3
+        else:
+            total = 64.0
+        groups = _math.ceil(self.n_features_in_ / model.features_per_group) + 1
+        pol = pol.resolve(n_context_rows=self.X_train_.shape[0], n_groups=groups, nlayers=model.nlayers,
+                          embed_dim=model.embed_dim, head_dim=model.embed_dim // model.nhead, device_total_gb=total)
+        self.memory_policy_ = pol
+        if pol.rung == "subsample" and pol.dropped_context_rows > 0:
+            warnings.warn(f"context subsampled: {pol.dropped_context_rows} rows dropped to fit the cache budget",
+                          ContextSubsampledWarning, stacklevel=3)
+            rng = np.random.default_rng(self.random_state)
+            keep = np.sort(rng.choice(self.X_train_.shape[0], self.X_train_.shape[0] - pol.dropped_context_rows,
+                                      replace=False))
+            self.X_train_, self.y_train_ = self.X_train_[keep], self.y_train_[keep]
+        dtype = "int8" if pol.rung in ("resident_int8", "context_sharded_int8") or pol.cache_dtype == "int8" else "bf16"
+        if dtype == "int8" and pol.cache_dtype == "bf16":
+            warnings.warn("context cache stored int8 to fit the memory budget", CacheQuantizedWarning, stacklevel=3)
+        return dtype
 
     # ------------------------------------------------------------------ sklearn API
     def fit(self, X, y):
@@ -125,6 +158,10 @@ class NoriRegressor(RegressorMixin, BaseEstimator):
         self.y_std_ = std if std > 0 else 1.0
         self.n_features_in_ = X.shape[1]
         self.context_ = None
+        self.predictor_ = None
+        from synthefy_nori_b200.inference.memory_policy import MemoryPolicy
+
+        MemoryPolicy.coerce(self.memory_policy)  # validate early (reference validates in fit)
         return self
 
     def _context(self):
@@ -183,12 +220,13 @@ class NoriRegressor(RegressorMixin, BaseEstimator):
     @property
     def memory_report_(self) -> dict:
         ctx = getattr(self, "context_", None)
-        return {
-            "cache_dtype": self.cache_dtype,
+        pol = getattr(self, "memory_policy_", None)
+        rep = pol.describe() if pol is not None else {}
+        rep.update({
             "cache_bytes": ctx.nbytes() if ctx is not None else 0,
             "context_rows": int(self.X_train_.shape[0]) if hasattr(self, "X_train_") else 0,
-            "dropped_rows": 0,
-        }
+        })
+        return rep
 
 
 def infer(X_train, y_train, X_test, *, model: str = "nori-6m", output_type: str = "mean", quantiles=None, **kw):
