@@ -62,3 +62,24 @@ def test_state_dict_round_trip_into_reference(reference_pkg):
     ours = build_model(dict(cfg))
     ref = ref_build(dict(cfg))
     ref.load_state_dict(ours.state_dict(), strict=True)
+
+
+def test_two_phase_v3_matches_reference(reference_pkg):
+    """Model v3 (nori-1-5 architecture family): two-phase encoder parity."""
+    from synthefy_nori.utils.loading import build_model as ref_build
+
+    from synthefy_nori_b200.models.config import preset_config
+
+    cfg = preset_config("nori-tiny")
+    cfg["two_phase_config"] = {"target_tokens": 2, "row_layers": 1, "row_heads": 2, "row_hidden_dim": 96}
+    torch.manual_seed(0)
+    ref = ref_build(dict(cfg)).eval()
+    ours = build_model(dict(cfg)).eval()
+    ours.load_state_dict(ref.state_dict(), strict=True)
+    torch.manual_seed(5)
+    x = torch.randn(2, 60, 5)
+    y = torch.randn(2, 40)
+    with torch.no_grad():
+        r = ref(x, y, 40, task_type="reg")
+        o = ours(x, y, 40, task_type="reg")
+    torch.testing.assert_close(o, r, atol=1e-5, rtol=1e-5)
