@@ -312,6 +312,47 @@ __device__ __forceinline__ void load_tile_q8(uint8_t* tile, const int8_t* base, 
   }
 }
 
+// Register-staged int8 tile loads: fetch the next tile's raw bytes and scales while the
+// current tile computes, then dequantise into shared memory (4 chunks of 8 values per
+// thread per tile with 128 threads).
+struct Q8Stage {
+  uint2 raw[4];
+  float sc[4];
+};
+
+__device__ __forceinline__ void q8_fetch(Q8Stage& st, const int8_t* base, const float* sbase, int64_t row_stride,
+                                         int64_t srow, int row0, int n_valid, int d_valid, int tid) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = tid + k * kAttnThreads;
+    const int r = i >> 3, c = i & 7;
+    const int gr = row0 + r;
+    if (gr < n_valid && c * 8 < d_valid) {
+      st.raw[k] = *reinterpret_cast<const uint2*>(base + static_cast<int64_t>(gr) * row_stride + c * 8);
+      st.sc[k] = sbase[static_cast<int64_t>(gr) * srow];
+    } else {
+      st.raw[k] = make_uint2(0u, 0u);
+      st.sc[k] = 0.f;
+    }
+  }
+}
+
+__device__ __forceinline__ void q8_commit(const Q8Stage& st, uint8_t* tile, int tid) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = tid + k * kAttnThreads;
+    const int r = i >> 3, c = i & 7;
+    const uint32_t lo = st.raw[k].x, hi = st.raw[k].y;
+    const float sc = st.sc[k];
+    auto cvt = [&](uint32_t word, int byte) -> float {
+      return static_cast<float>(static_cast<int8_t>((word >> (8 * byte)) & 0xFFu)) * sc;
+    };
+    *reinterpret_cast<uint4*>(tile + swz(r, c)) =
+        make_uint4(pack_bf16x2(cvt(lo, 0), cvt(lo, 1)), pack_bf16x2(cvt(lo, 2), cvt(lo, 3)),
+                   pack_bf16x2(cvt(hi, 0), cvt(hi, 1)), pack_bf16x2(cvt(hi, 2), cvt(hi, 3)));
+  }
+}
+
 __global__ void __launch_bounds__(kAttnThreads) attn_fwd_q8_kernel(AttnQ8Params p) {
   __shared__ __align__(128) uint8_t sq[kBlkQ * 128];
   __shared__ __align__(128) uint8_t sk[kBlkK * 128];
@@ -752,22 +793,48 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_q8_shards_kernel(AttnSh
   const int64_t i0 = t / p.lkv.d1;
   FwdState st;
   bool init = false;
-  for (int sh = 0; sh < p.n_shards; ++sh) {
-    const int nk = p.nk[sh];
-    const int8_t* kb = p.kv[sh] + i0 * p.kv_s0[sh] + i1 * p.lkv.s1 + i2 * p.lkv.s2;
-    const float* ksb = p.sc[sh] + i0 * p.sc_s0[sh] + i1 * p.ls.s1 + i2 * p.ls.s2;
-    const int n_tiles = (nk + kBlkK - 1) / kBlkK;
-    for (int tt = 0; tt < n_tiles; ++tt) {
-      load_tile_q8(sk, kb, ksb, p.lkv.row, p.ls.row, tt * kBlkK, nk, p.d_valid, tid, kAttnThreads);
-      load_tile_q8(sv, kb + p.E, ksb + p.H, p.lkv.row, p.ls.row, tt * kBlkK, nk, p.d_valid, tid, kAttnThreads);
-      __syncthreads();
-      if (!init) {
-        fwd_init(st, sq, warp, lane);
-        init = true;
-      }
-      fwd_tile(st, sk, sv, tt * kBlkK, nk, p.scale_log2, lane);
-      __syncthreads();
+  // flatten (shard, tile) into one sequence and prefetch one step ahead
+  auto shard_base = [&](int sh, const int8_t*& kb, const float*& ksb) {
+    kb = p.kv[sh] + i0 * p.kv_s0[sh] + i1 * p.lkv.s1 + i2 * p.lkv.s2;
+    ksb = p.sc[sh] + i0 * p.sc_s0[sh] + i1 * p.ls.s1 + i2 * p.ls.s2;
+  };
+  int sh = 0, tt = 0;
+  while (sh < p.n_shards && p.nk[sh] == 0) ++sh;
+  Q8Stage nk_st, nv_st;
+  if (sh < p.n_shards) {
+    const int8_t* kb;
+    const float* ksb;
+    shard_base(sh, kb, ksb);
+    q8_fetch(nk_st, kb, ksb, p.lkv.row, p.ls.row, 0, p.nk[sh], p.d_valid, tid);
+    q8_fetch(nv_st, kb + p.E, ksb + p.H, p.lkv.row, p.ls.row, 0, p.nk[sh], p.d_valid, tid);
+  }
+  while (sh < p.n_shards) {
+    const int cur_nk = p.nk[sh], cur_t = tt;
+    q8_commit(nk_st, sk, tid);
+    q8_commit(nv_st, sv, tid);
+    // advance to the next (shard, tile) and start its loads before computing this one
+    int nsh = sh, ntt = tt + 1;
+    if (ntt * kBlkK >= cur_nk) {
+      ntt = 0;
+      ++nsh;
+      while (nsh < p.n_shards && p.nk[nsh] == 0) ++nsh;
     }
+    if (nsh < p.n_shards) {
+      const int8_t* kb;
+      const float* ksb;
+      shard_base(nsh, kb, ksb);
+      q8_fetch(nk_st, kb, ksb, p.lkv.row, p.ls.row, ntt * kBlkK, p.nk[nsh], p.d_valid, tid);
+      q8_fetch(nv_st, kb + p.E, ksb + p.H, p.lkv.row, p.ls.row, ntt * kBlkK, p.nk[nsh], p.d_valid, tid);
+    }
+    __syncthreads();
+    if (!init) {
+      fwd_init(st, sq, warp, lane);
+      init = true;
+    }
+    fwd_tile(st, sk, sv, cur_t * kBlkK, cur_nk, p.scale_log2, lane);
+    __syncthreads();
+    sh = nsh;
+    tt = ntt;
   }
   if (init) fwd_store(st, p.o + p.lo.offset(bh, 0), p.lo.row, p.lse, bh, q0, p.Nq, p.d_valid, warp, lane);
 }

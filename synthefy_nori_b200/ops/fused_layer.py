@@ -590,8 +590,9 @@ def _seq_query_forward(layer, w, x, kv: NativeKV, g: Geometry, lse=None, partial
     if kv.quantized:
         l2 = _seq_layout(g.ep, g, 2 * E)
         ls = (g.ep * g.T * 2 * g.H, 2 * g.H, 1, g.T * 2 * g.H, g.T, g.H)
-        ops.attention_fwd_q8(q, kv.kv, kv.scale, o, lq=lq, lkv=l2, lscale=ls, lo=lq, BH=BTH, Nq=g.nq, Nk=g.ep, d=D,
-                             scale=1.0 / math.sqrt(D), lse=lse)
+        # one-shard case of the multi-shard kernel (register-pipelined int8 tile loads)
+        ops.lib().attn_fwd_q8_shards(q, [kv.kv.data_ptr()], [kv.scale.data_ptr()], [g.ep], [l2[0]], [ls[0]], o, lse,
+                                     list(lq), list(l2), list(ls), list(lq), E, g.H, BTH, g.nq, D, 1.0 / math.sqrt(D))
     else:
         l2 = _seq_layout(g.ep, g, 2 * E)
         _attn(q, kv.kv[:, :E], kv.kv[:, E:], o, lq, l2, lq, BTH, g.nq, g.ep, D, lse=lse)
