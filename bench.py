@@ -381,6 +381,19 @@ def run_infer4(args, device, world, rank, impl):
     torch.manual_seed(args.seed)
     model = mk(dict(preset_config(args.model))).to(device).eval()
     X, y = _infer_tables(1, n_ctx, n_q, 100, args.seed, device, nan_frac=0.10, n_cat=20)
+    # warm-up (kernel attributes, tensor maps, allocator) on a small slice, untimed
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16, enabled=impl == "reference"):
+        if world > 1:
+            from synthefy_nori_b200.parallel.context_parallel import ShardedContextPredictor
+
+            wsp = ShardedContextPredictor(model, device)
+            wsp.build(X[:, :512], y[:, :512])
+            wsp.predict_raw(X[:, n_ctx : n_ctx + 64])
+            wsp.close()
+        else:
+            wc = model.build_context_cache(X[:, :512], y[:, :512], cache_dtype="int8")
+            model.apply_context_cache(X[:, n_ctx : n_ctx + 64], wc)
+            del wc
     if world > 1 and impl == "reference":
         raise SystemExit("the reference has no multi-GPU context path; run --impl reference with one GPU")
     torch.cuda.synchronize(device)
