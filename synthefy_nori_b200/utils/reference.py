@@ -19,6 +19,13 @@ _REPO = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__
 REF_DIR = os.path.join(_REPO, "baseline", "_ref")
 
 
+class _Unavailable:
+    """Placeholder for a class of a missing optional dependency; using it raises."""
+
+    def __init__(self, *a, **k):
+        raise ImportError("optional dependency of the reference is not installed in this image")
+
+
 def import_reference():
     """Return the reference ``synthefy_nori`` module, or ``None`` if not installed."""
     if not os.path.isdir(os.path.join(REF_DIR, "synthefy_nori")):
@@ -30,7 +37,10 @@ def import_reference():
             try:
                 __import__(name)
             except ImportError:
-                sys.modules[name] = types.ModuleType(name)
+                stub = types.ModuleType(name)
+                if name == "kditransform":
+                    stub.KDITransformer = _Unavailable
+                sys.modules[name] = stub
     import synthefy_nori  # noqa: F401
 
     return synthefy_nori
