@@ -37,3 +37,23 @@ def test_regressor_cuda_matches_cpu():
     qa = cpu.predict(X[100:], output_type="quantiles", quantiles=[0.1, 0.9])
     qb = gpu.predict(X[100:], output_type="quantiles", quantiles=[0.1, 0.9])
     assert np.max(np.abs(qa - qb)) < 0.08 * np.std(y) + 1e-3
+
+
+def test_default_ensemble_cuda_matches_cpu():
+    """Eight reference-config members (quantile / adaptive rebalancing, SVD features,
+    fingerprint, shuffles) preprocessed on the device, batched by width."""
+    from synthefy_nori_b200.api import NoriRegressor
+
+    rng = np.random.default_rng(1)
+    X = rng.standard_normal((300, 9)).astype(np.float32)
+    X[:, 2] = np.exp(X[:, 2])
+    X[rng.random(X.shape) < 0.05] = np.nan
+    y = np.nan_to_num(X) @ rng.standard_normal(9) + 0.1 * rng.standard_normal(300)
+    kw = dict(model="nori-tiny", weights="random")
+    cpu = NoriRegressor(device="cpu", **kw).fit(X[:240], y[:240])
+    gpu = NoriRegressor(device="cuda", **kw).fit(X[:240], y[:240])
+    a, b = cpu.predict(X[240:]), gpu.predict(X[240:])
+    assert gpu.predictor_.n_estimators == 8
+    assert np.max(np.abs(a - b)) < 0.05 * np.std(y) + 1e-3
+    e = gpu.get_embeddings(X[240:])
+    assert e.shape[:2] == (8, 60) and np.all(np.isfinite(e))
