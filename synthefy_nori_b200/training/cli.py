@@ -53,6 +53,10 @@ def parse_args(argv=None):
     ap.add_argument("--pinball-monotonicity-weight", type=float, default=0.05)
     ap.add_argument("--pinball-mse-weight", type=float, default=0.0)
     ap.add_argument("--grad-reduction", default="peer", choices=["peer", "nccl"])
+    ap.add_argument("--optimizer", default="adamw", choices=["adamw", "muon"])
+    ap.add_argument("--muon-include-nd", action="store_true")
+    ap.add_argument("--loss", default="pinball", choices=["pinball", "mse", "smooth_l1", "huber", "bar_distribution"])
+    ap.add_argument("--loss-spike-factor", type=float, default=10.0, help="skip steps above this x loss EMA (0: off)")
     ap.add_argument("--checkpoint-dir", default=None)
     ap.add_argument("--save-interval", type=int, default=1000)
     ap.add_argument("--resume", default=None, help="checkpoint file to resume from ('latest' = checkpoint-dir)")
@@ -101,7 +105,9 @@ class Run:
         model = build_model(dict(self.model_config))
         self.tcfg = TrainConfig(lr=args.lr, weight_decay=args.weight_decay, ema_decay=args.ema_decay,
                                 pinball_monotonicity_weight=args.pinball_monotonicity_weight,
-                                pinball_mse_weight=args.pinball_mse_weight, grad_reduction=args.grad_reduction)
+                                pinball_mse_weight=args.pinball_mse_weight, grad_reduction=args.grad_reduction,
+                                optimizer=args.optimizer, muon_include_nd=args.muon_include_nd, loss=args.loss,
+                                loss_spike_factor=args.loss_spike_factor or None)
         self.trainer = NoriTrainer(model, self.tcfg, device)
         self.prior = PriorConfig(min_rows=args.min_rows, max_rows=args.max_rows, min_features=args.min_features,
                                  max_features=args.max_features, pad_features=args.max_features)
@@ -135,15 +141,20 @@ class Run:
             names = {p.data_ptr(): n for n, p in tr.model.named_parameters()}
             for p, o in zip(flat.params, flat.offsets):
                 ema_sd[names[p.data_ptr()]] = ema[o : o + p.numel()].view(p.shape).detach().cpu()
+        extra = {}
+        if tr.muon is not None:
+            extra["muon_momentum"] = [b.detach().cpu() for _, _, b in tr.muon.groups]
         return {
             "model_config": self.model_config,
             "model_state_dict": sd,
             "ema_state_dict": ema_sd,
             "optimizer_state": {"m": m.detach().cpu(), "v": v.detach().cpu(),
-                                "ema": ema.detach().cpu() if ema is not None else None, "step": step},
+                                "ema": ema.detach().cpu() if ema is not None else None, "step": step, **extra},
             "step": self.step,
             "training_config": dataclasses.asdict(self.tcfg) | {"argv": vars(self.args)},
             "rng_state": {"shape": self.shape_rng.get_state(), "torch": torch.get_rng_state()},
+            "trainer_state": {"loss_ema": None if tr.loss_ema is None else float(tr.loss_ema),
+                              "steps_done": tr.steps_done, "skipped_steps": tr.skipped_steps},
         }
 
     def _gather_shards(self, shard: torch.Tensor) -> torch.Tensor:
@@ -175,7 +186,15 @@ class Run:
             if tr.opt.ema is not None and o["ema"] is not None:
                 tr.opt.ema.copy_(o["ema"])
             tr.opt.step_count = int(o["step"])
+            if tr.muon is not None:
+                for (_, _, b), src in zip(tr.muon.groups, o["muon_momentum"]):
+                    b.copy_(src)
         self.step = int(ckpt["step"])
+        ts = ckpt.get("trainer_state") or {}
+        if ts.get("loss_ema") is not None:
+            tr.loss_ema = torch.tensor(ts["loss_ema"], device=self.device)
+        tr.steps_done = int(ts.get("steps_done", 0))
+        tr.skipped_steps = int(ts.get("skipped_steps", 0))
         self.shape_rng.set_state(ckpt["rng_state"]["shape"])
         torch.set_rng_state(ckpt["rng_state"]["torch"])
         bump_weight_generation()
