@@ -1,0 +1,96 @@
+"""Nori-TS: probabilistic forecasting as per-series tabular regression with Nori.
+
+Parity target: reference ``libs/synthefy/src/synthefy/nori_ts/core.py:83-470``.  Each
+series' history rows (at most ``context_length``, the most recent) and its horizon rows
+become one table: features are time features (running index, calendar sin/cos, FFT
+seasonal periods) plus any covariate columns; the horizon rows carry known future
+features and no target.  The model regresses target on features and returns quantiles;
+the point forecast is the median.  Series are independent requests (no pooling across
+series).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pandas as pd
+
+from synthefy_nori_b200.nori_ts.features import (AutoSeasonalFeature, CalendarFeature, RunningIndexFeature,
+                                                 default_features, seasonal_periods)
+
+DEFAULT_QUANTILES = [0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9]
+TARGET = "target"
+
+
+def _check_frame(df: pd.DataFrame, name: str) -> pd.DataFrame:
+    if not isinstance(df, pd.DataFrame) or list(df.index.names) != ["item_id", "timestamp"]:
+        raise ValueError(f"{name} must be a DataFrame indexed by (item_id, timestamp)")
+    return df if df.index.is_monotonic_increasing else df.sort_index()
+
+
+class NoriTSForecaster:
+    """``client``: any object with ``predict(X_train, y_train, X_test, output_type="quantiles",
+    quantiles=...)`` (``SynthefyNoriClient``); without one, a local client is built from
+    ``regressor_kwargs`` (e.g. ``model="nori-6m", weights=...``)."""
+
+    def __init__(self, *, client=None, context_length: int = 4096, quantiles=None, features=None,
+                 **regressor_kwargs):
+        if client is None:
+            if not regressor_kwargs.get("model") and not regressor_kwargs.get("model_path"):
+                raise ValueError("pass client= or a model= / model_path= for the local client")
+            from synthefy_nori_b200.client import SynthefyNoriClient
+
+            client = SynthefyNoriClient(mode="local", **regressor_kwargs)
+        if not callable(getattr(client, "predict", None)):
+            raise ValueError("client must expose predict()")
+        self.client = client
+        self.context_length = context_length
+        self.quantiles = sorted(quantiles if quantiles is not None else DEFAULT_QUANTILES)
+        self.features = features if features is not None else default_features()
+
+    def _featurize(self, train: pd.DataFrame, test: pd.DataFrame) -> tuple[pd.DataFrame, pd.DataFrame]:
+        both = pd.concat([train.assign(_hist=True), test.assign(_hist=False)]).sort_index()
+        hist = both["_hist"].to_numpy(bool)
+        both = both.drop(columns="_hist")
+        for f in self.features:
+            both = f(both, hist) if isinstance(f, AutoSeasonalFeature) else f(both)
+        return both[hist], both[~hist]
+
+    def predict(self, train_df: pd.DataFrame, test_df: pd.DataFrame) -> pd.DataFrame:
+        train_df, test_df = _check_frame(train_df, "train_df"), _check_frame(test_df, "test_df")
+        hist_ids = set(train_df.index.get_level_values("item_id"))
+        missing = [i for i in pd.unique(test_df.index.get_level_values("item_id")) if i not in hist_ids]
+        if missing:
+            raise ValueError(f"{len(missing)} series have horizon rows but no history (ids {missing[:5]})")
+        if self.context_length and self.context_length > 0:
+            train_df = train_df.groupby(level="item_id", group_keys=False).tail(self.context_length)
+        if TARGET not in test_df:
+            test_df = test_df.assign(**{TARGET: np.nan})
+        tr, te = self._featurize(train_df, test_df)
+        qs = list(self.quantiles) if 0.5 in self.quantiles else sorted(self.quantiles + [0.5])
+        out = []
+        for item, te_i in te.groupby(level="item_id", sort=False):
+            tr_i = tr.xs(item, level="item_id", drop_level=False)
+            tr_i = tr_i[np.isfinite(tr_i[TARGET].to_numpy(np.float64))]
+            Xtr = tr_i.drop(columns=[TARGET]).to_numpy(np.float32)
+            Xte = te_i.drop(columns=[TARGET]).to_numpy(np.float32)
+            q = np.asarray(self.client.predict(Xtr, tr_i[TARGET].to_numpy(np.float64), Xte, output_type="quantiles",
+                                               quantiles=qs))
+            q = np.sort(q, axis=0)  # [len(qs), horizon], monotone in the level
+            frame = pd.DataFrame({str(l): q[k] for k, l in enumerate(qs) if l in self.quantiles}, index=te_i.index)
+            frame.insert(0, TARGET, q[qs.index(0.5)])
+            out.append(frame)
+        return pd.concat(out).loc[test_df.index]
+
+    def predict_df(self, context_df: pd.DataFrame, future_df: pd.DataFrame, *, id_column="item_id",
+                   timestamp_column="timestamp", target_column="target") -> pd.DataFrame:
+        """Flat-frame convenience: columns ``item_id``, ``timestamp``, target (+ covariates)."""
+        def idx(df):
+            d = df.rename(columns={id_column: "item_id", timestamp_column: "timestamp", target_column: TARGET})
+            d["timestamp"] = pd.to_datetime(d["timestamp"])
+            return d.set_index(["item_id", "timestamp"]).sort_index()
+
+        return self.predict(idx(context_df), idx(future_df)).reset_index()
+
+
+__all__ = ["NoriTSForecaster", "RunningIndexFeature", "CalendarFeature", "AutoSeasonalFeature", "seasonal_periods",
+           "default_features", "DEFAULT_QUANTILES"]
