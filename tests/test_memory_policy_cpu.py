@@ -55,5 +55,7 @@ def test_client_local_mode_and_multi_target():
     c = SynthefyNoriClient(mode="local", model="nori-tiny", weights="random", device="cpu")
     out = c.predict(X[:50], Y[:50], X[50:])
     assert out.shape == (10, 2)
-    with pytest.raises(RuntimeError):
-        SynthefyNoriClient(mode="remote")
+    with pytest.raises(ValueError):
+        SynthefyNoriClient(mode="remote")  # no model named
+    with pytest.raises(ValueError):
+        SynthefyNoriClient(mode="remote", model="nori-6m", api_key="")  # no key
