@@ -52,3 +52,55 @@ def test_handle_exchange_and_flat_allreduce_on_gloo():
         assert ranks == [0, 1] and first == [0, 1]
     means = [r[2] for r in res if r[1] == "mean"]
     assert means == [1.5, 1.5]
+
+
+def _dp_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import numpy as np
+
+        from synthefy_nori_b200.inference.predictor import NoriPredictor
+        from synthefy_nori_b200.models.config import preset_config
+        from synthefy_nori_b200.parallel.distributed_inference import DistributedInference, table_parallel_predict
+        from synthefy_nori_b200.utils.loading import build_model
+
+        torch.manual_seed(0)
+        model = build_model(preset_config("nori-tiny")).eval()
+        rng = np.random.default_rng(0)
+        X = rng.standard_normal((47, 4)).astype(np.float32)
+        y = X[:, 0].copy()
+        pred = NoriPredictor(model, "cpu", n_estimators=1)
+        ctx = pred.fit_context(X[:30], y[:30])
+        full = pred.predict_raw(ctx, X[30:])
+        got = DistributedInference(pred).predict_raw(ctx, torch.from_numpy(X[30:]))
+        q.put((rank, "query", float((got - full).abs().max())))
+        xt = torch.from_numpy(rng.standard_normal((3, 40, 4)).astype(np.float32))
+        yt = xt[..., 0].clone()
+        ref = model.apply_context_cache(xt[:, 30:], model.build_context_cache(xt[:, :30], yt[:, :30])).float()
+        tp = table_parallel_predict(model, xt[:, :30], yt[:, :30], xt[:, 30:])
+        q.put((rank, "tables", float((tp - ref).abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_distributed_inference_on_gloo():
+    import socket
+
+    world = 2
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_dp_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=240) for _ in range(2 * world)]
+    for p in ps:
+        p.join(timeout=60)
+    assert all(p.exitcode == 0 for p in ps)
+    assert all(v < 1e-5 for _, _, v in res), res
