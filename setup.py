@@ -31,7 +31,14 @@ sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(glob.glob(os.pa
 setup(
     name="synthefy_nori_b200",
     version="0.1.0",
-    packages=["synthefy_nori_b200"],
+    packages=[d.replace(os.sep, ".") for d, _, files in os.walk("synthefy_nori_b200") if "__init__.py" in files],
+    entry_points={"console_scripts": [
+        "synthefy-nori-b200-train = synthefy_nori_b200.training.cli:main",
+        "synthefy-nori-b200-eval = synthefy_nori_b200.evaluation.cli:main",
+        "synthefy-nori-b200-download = synthefy_nori_b200.hf:download_cli",
+        "synthefy-nori-b200-upload = synthefy_nori_b200.hf:upload_cli",
+        "synthefy-nori-b200-serve = synthefy_nori_b200.serving:main",
+    ]},
     ext_modules=[
         CUDAExtension(
             name="synthefy_nori_b200._C",

@@ -3,9 +3,12 @@
 // self-attention and query->context cross-attention per (table, column, head)
 // (reference model/layer.py:1407-1441, 685-745).
 //
-// One CTA = 128 query rows of one head. Warp roles (256 threads):
-//   warp 0      TMA producer: the Q tile once, then 128-key K / V tiles into a
-//               2-stage ring (5-D tensor maps read the strided token-major layouts
+// Persistent: one CTA per SM loops over work items (one item = 128 query rows of one
+// head); TMEM, barriers and the K / V pipeline carry over from item to item, so the next
+// item's Q and K / V loads overlap the current item's last tiles.  Warp roles (384 threads):
+//   warp 0      TMA producer: the Q tile once, then 128-key K and V tiles into two
+//               3-stage rings (K(j) is released when S_j completes, V(j) when O_j
+//               completes; 5-D tensor maps read the strided token-major layouts
 //               directly; head-dim padding and tails are zero-filled by TMA);
 //   warp 1      TMEM owner + MMA issuer: S_j = Q K_j^T (M=128, N=128, K=64) into one
 //               of two TMEM score buffers, then O_j = P_j V_j (M=128, N=64, K=128,
@@ -39,14 +42,16 @@ constexpr int kThreads = 384;  // warps 0 (TMA), 1 (MMA), 4..11 (softmax)
 constexpr int kSoftmaxWarps = 8;  // softmax-side barriers take one arrive per warp
 constexpr int kTileBytes = kM * kD * 2;  // 16 KB (Q, K or V tile)
 constexpr int kPBytes = kM * kN * 2;     // 32 KB (P tile: two 64-key panels)
-// smem: Q | K[2] | V[2] | P[2] | barriers
-constexpr int kSmemBytes = kTileBytes * 5 + kPBytes * 2 + 1024 + 256;
+constexpr int kStages = 3;  // K and V rings (separate: K(j) frees after S_j, V(j) after O_j)
+// smem: Q[2] | K[3] | V[3] | P[2] | barriers
+constexpr int kSmemBytes = kTileBytes * (2 + 2 * kStages) + kPBytes * 2 + 1024 + 256;
 constexpr uint32_t kTmemCols = 512;  // S[2] (2 x 128) + O[2] (2 x 64) -> 384 used
 }  // namespace fa
 
 struct AttnTcParams {
   int Nq, Nk, d_valid;
   int n_tiles_q;
+  int64_t n_items;  // BH * n_tiles_q work items (head, query tile), visited with stride gridDim.x
   float scale_log2;
   // coordinate positions (inside the 5-D maps) of row / i2 / i1 / i0 for Q and for K/V
   int q_pos[4], kv_pos[4];
@@ -92,47 +97,51 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   using namespace fa;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kTileBytes;            // 2 stages
-  uint8_t* sV = sK + 2 * kTileBytes;        // 2 stages
-  uint8_t* sP = sV + 2 * kTileBytes;        // 2 buffers of 32 KB
+  uint8_t* sQ = smem;                             // 2 buffers (consecutive work items)
+  uint8_t* sK = sQ + 2 * kTileBytes;              // kStages
+  uint8_t* sV = sK + kStages * kTileBytes;        // kStages
+  uint8_t* sP = sV + kStages * kTileBytes;        // 2 buffers of 32 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* p_full = bars + 7;    // [2]
-  uint64_t* o_full = bars + 9;    // [2]
-  uint64_t* o_free = bars + 11;   // [2]
-  uint64_t* xbar = bars + 13;     // [2] row-max exchange between the two column halves
-  uint64_t* sbar = bars + 15;     // row-sum exchange at the end
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* q_full = bars;        // [2]
+  uint64_t* q_empty = bars + 2;   // [2]
+  uint64_t* s_full = bars + 4;    // [2]
+  uint64_t* p_full = bars + 6;    // [2]
+  uint64_t* o_full = bars + 8;    // [2]
+  uint64_t* o_free = bars + 10;   // [2]
+  uint64_t* xbar = bars + 12;     // [2] row-max exchange between the two column halves
+  uint64_t* sbar = bars + 14;     // [2] row-sum exchange at the end of a work item
+  uint64_t* k_full = bars + 16;   // [kStages]
+  uint64_t* k_empty = bars + 19;  // [kStages]
+  uint64_t* v_full = bars + 22;   // [kStages]
+  uint64_t* v_empty = bars + 25;  // [kStages]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  __shared__ float red_max[2][2][kM];  // [iteration parity][column half][row]
-  __shared__ float red_sum[2][kM];
+  __shared__ float red_max[2][2][kM];  // [tile parity][column half][row]
+  __shared__ float red_sum[2][2][kM];  // [item parity][column half][row]
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int64_t bh = blockIdx.x / p.n_tiles_q;
-  const int q0 = static_cast<int>(blockIdx.x % p.n_tiles_q) * kM;
-  const int i2 = static_cast<int>(bh % p.d2);
-  const int i1 = static_cast<int>((bh / p.d2) % p.d1);
-  const int i0 = static_cast<int>(bh / (static_cast<int64_t>(p.d1) * p.d2));
   const int n_tiles = (p.Nk + kN - 1) / kN;
+  const int64_t n_items = p.n_items;
   // a CTA that starts after another one timed out returns at once
   if (p.status != nullptr && *reinterpret_cast<volatile int*>(p.status) != 0) return;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], kSoftmaxWarps);
       mbar_init(&o_full[i], 1);
       mbar_init(&o_free[i], kSoftmaxWarps);
       mbar_init(&xbar[i], kSoftmaxWarps);
+      mbar_init(&sbar[i], kSoftmaxWarps);
     }
-    mbar_init(sbar, kSoftmaxWarps);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -144,59 +153,108 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   const uint32_t tS = tmem;            // S buffers at columns 0, 128
   const uint32_t tO = tmem + 2 * kN;   // O buffers at columns 256, 320
 
+  // work item w -> (head bh, query tile); items are visited with stride gridDim.x
+  auto item_coords = [&](int64_t w, int& q0, int& i2, int& i1, int& i0, int64_t& bh) {
+    bh = w / p.n_tiles_q;
+    q0 = static_cast<int>(w % p.n_tiles_q) * kM;
+    i2 = static_cast<int>(bh % p.d2);
+    i1 = static_cast<int>((bh / p.d2) % p.d1);
+    i0 = static_cast<int>(bh / (static_cast<int64_t>(p.d1) * p.d2));
+  };
+
   if (warp == 0) {
     if (elect_one()) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       int c[5];
-      coords_for(p.q_pos, q0, i2, i1, i0, c);
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      tma_load_5d(sQ, &tmQ, q_full, c);
-      for (int j = 0; j < n_tiles; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, p.status, kTimeoutProducer, abort_flag)) break;
-        coords_for(p.kv_pos, j * kN, i2, i1, i0, c);
-        mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
-        tma_load_5d(sK + s * kTileBytes, &tmK, &kv_full[s], c);
-        tma_load_5d(sV + s * kTileBytes, &tmV, &kv_full[s], c);
+      int64_t gk = 0, gv = 0;  // global K / V tile counters (ring positions)
+      int it = 0;
+      bool pok = true;
+      for (int64_t w = blockIdx.x; pok && w < n_items; w += gridDim.x, ++it) {
+        int q0, i2, i1, i0;
+        int64_t bh;
+        item_coords(w, q0, i2, i1, i0, bh);
+        const int qb = it & 1;
+        if (!mbar_wait(&q_empty[qb], ((it >> 1) & 1) ^ 1, p.status, kTimeoutProducer, abort_flag)) break;
+        coords_for(p.q_pos, q0, i2, i1, i0, c);
+        mbar_arrive_expect_tx(&q_full[qb], kTileBytes);
+        tma_load_5d(sQ + qb * kTileBytes, &tmQ, &q_full[qb], c);
+        // K(j) can be reloaded once S_j is done, V(j) once O_j is done; K runs one tile
+        // ahead of V so a slow V slot never holds back the next score tile
+        auto load_k = [&](int j) -> bool {
+          const int st = static_cast<int>(gk % kStages);
+          if (!mbar_wait(&k_empty[st], ((gk / kStages) & 1) ^ 1, p.status, kTimeoutProducer, abort_flag)) return false;
+          coords_for(p.kv_pos, j * kN, i2, i1, i0, c);
+          mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+          tma_load_5d(sK + st * kTileBytes, &tmK, &k_full[st], c);
+          ++gk;
+          return true;
+        };
+        pok = load_k(0);
+        for (int j = 0; pok && j < n_tiles; ++j) {
+          if (j + 1 < n_tiles && !(pok = load_k(j + 1))) break;
+          const int st = static_cast<int>(gv % kStages);
+          if (!(pok = mbar_wait(&v_empty[st], ((gv / kStages) & 1) ^ 1, p.status, kTimeoutProducer, abort_flag)))
+            break;
+          coords_for(p.kv_pos, j * kN, i2, i1, i0, c);
+          mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+          tma_load_5d(sV + st * kTileBytes, &tmV, &v_full[st], c);
+          ++gv;
+        }
       }
     }
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(kM, kN, false, false);
       constexpr uint32_t idesc_o = umma_idesc_bf16(kM, kD, false, true);
-      const uint32_t aQ = smem_u32(sQ);
-      bool ok = mbar_wait(q_full, 0, p.status, kTimeoutMma, abort_flag);
-      auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, p.status, kTimeoutMma, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t bK = smem_u32(sK + s * kTileBytes);
+      int64_t gk = 0, gv = 0, gt = 0;  // K / V ring positions, global tile index (S / P / O buffers)
+      int it = 0;
+      bool ok = true;
+      for (int64_t w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
+        const int qb = it & 1;
+        if (!(ok = mbar_wait(&q_full[qb], (it >> 1) & 1, p.status, kTimeoutMma, abort_flag))) break;
+        const uint32_t aQ = smem_u32(sQ + qb * kTileBytes);
+        const int64_t t0 = gt;  // global index of this item's first tile
+        auto issue_s = [&](int64_t g) -> bool {
+          const int s = static_cast<int>(g & 1), st = static_cast<int>(gk % kStages);
+          if (!mbar_wait(&k_full[st], (gk / kStages) & 1, p.status, kTimeoutMma, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t bK = smem_u32(sK + st * kTileBytes);
 #pragma unroll
-        for (int k = 0; k < kD / 16; ++k)
-          umma_bf16_ss(tS + s * kN, umma_desc_kmajor_sw128(aQ + k * 32), umma_desc_kmajor_sw128(bK + k * 32), idesc_s,
-                       k > 0 ? 1u : 0u);
-        umma_commit(&s_full[s]);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int s = j & 1;
-        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        if (!mbar_wait(&p_full[s], (j >> 1) & 1, p.status, kTimeoutMma, abort_flag)) break;
-        if (j >= 2 && !mbar_wait(&o_free[s], ((j >> 1) & 1) ^ 1, p.status, kTimeoutMma, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t aP = smem_u32(sP + s * kPBytes);
-        const uint32_t bV = smem_u32(sV + s * kTileBytes);
+          for (int k = 0; k < kD / 16; ++k)
+            umma_bf16_ss(tS + s * kN, umma_desc_kmajor_sw128(aQ + k * 32), umma_desc_kmajor_sw128(bK + k * 32),
+                         idesc_s, k > 0 ? 1u : 0u);
+          umma_commit(&s_full[s]);
+          umma_commit(&k_empty[st]);
+          ++gk;
+          return true;
+        };
+        ok = issue_s(t0);
+        for (int j = 0; ok && j < n_tiles; ++j, ++gt) {
+          const int s = static_cast<int>(gt & 1);
+          if (j + 1 < n_tiles) {
+            if (!(ok = issue_s(gt + 1))) break;
+          } else {
+            umma_commit(&q_empty[qb]);  // the item's last score MMA read Q
+          }
+          const int st = static_cast<int>(gv % kStages);
+          if (!(ok = mbar_wait(&p_full[s], (gt >> 1) & 1, p.status, kTimeoutMma, abort_flag))) break;
+          if (gt >= 2 && !(ok = mbar_wait(&o_free[s], ((gt >> 1) & 1) ^ 1, p.status, kTimeoutMma, abort_flag))) break;
+          if (!(ok = mbar_wait(&v_full[st], (gv / kStages) & 1, p.status, kTimeoutMma, abort_flag))) break;
+          tc_fence_after();
+          const uint32_t aP = smem_u32(sP + s * kPBytes);
+          const uint32_t bV = smem_u32(sV + st * kTileBytes);
 #pragma unroll
-        for (int k = 0; k < kN / 16; ++k) {
-          const uint64_t da = umma_desc_kmajor_sw128(aP + (k >> 2) * (kM * 128) + (k & 3) * 32);
-          const uint64_t db = umma_smem_desc(bV + k * 2048, 8192, 1024, 2);
-          umma_bf16_ss(tO + s * kD, da, db, idesc_o, k > 0 ? 1u : 0u);
+          for (int k = 0; k < kN / 16; ++k) {
+            const uint64_t da = umma_desc_kmajor_sw128(aP + (k >> 2) * (kM * 128) + (k & 3) * 32);
+            const uint64_t db = umma_smem_desc(bV + k * 2048, 8192, 1024, 2);
+            umma_bf16_ss(tO + s * kD, da, db, idesc_o, k > 0 ? 1u : 0u);
+          }
+          umma_commit(&o_full[s]);
+          umma_commit(&v_empty[st]);
+          ++gv;
         }
-        umma_commit(&o_full[s]);
-        umma_commit(&kv_empty[s]);
       }
     }
   } else if (warp >= 4) {
@@ -207,131 +265,140 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
     const int half = (warp - 4) >> 2;
     const int r = q * 32 + lane;  // row in tile == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    float m_cur = -INFINITY, l = 0.f;
-    float o[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) o[i] = 0.f;
     bool ok = true;
-    auto absorb = [&](int j, float a) -> bool {
-      const int s = j & 1;
-      if (!mbar_wait_warp(&o_full[s], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) return false;
-      tc_fence_after();
-      uint32_t v[32];
-      tmem_ld32(tO + s * kD + lane_off + half * 32, v);
-      tmem_wait_ld();
+    int64_t gt = 0;  // global tile index (matches the MMA warp's)
+    int it = 0;
+    for (int64_t w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
+      int q0, i2, i1, i0;
+      int64_t bh;
+      item_coords(w, q0, i2, i1, i0, bh);
+      float m_cur = -INFINITY, l = 0.f;
+      float o[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) o[i] = o[i] * a + __uint_as_float(v[i]);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free[s]);
-      return true;
-    };
-    float alpha_pending = 1.f;
-    for (int j = 0; ok && j < n_tiles; ++j) {
-      const int s = j & 1;
-      if (!mbar_wait_warp(&s_full[s], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int valid = min(kN, p.Nk - j * kN) - half * 64;  // valid columns of this half
-      const uint32_t ts = tS + s * kN + lane_off + half * 64;
-      uint32_t v0[32], v1[32];
-      tmem_ld32(ts, v0);
-      tmem_ld32(ts + 32, v1);
-      tmem_wait_ld();
-      const bool full_tile = valid >= 64;
-      float mx = -INFINITY;
-      if (full_tile) {
+      for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      auto absorb = [&](int64_t g, float a) -> bool {
+        const int s = static_cast<int>(g & 1);
+        if (!mbar_wait_warp(&o_full[s], (g >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) return false;
+        tc_fence_after();
+        uint32_t v[32];
+        tmem_ld32(tO + s * kD + lane_off + half * 32, v);
+        tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(__uint_as_float(v0[i]), __uint_as_float(v1[i])));
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (i < valid) mx = fmaxf(mx, __uint_as_float(v0[i]));
-          if (32 + i < valid) mx = fmaxf(mx, __uint_as_float(v1[i]));
+        for (int i = 0; i < 32; ++i) o[i] = o[i] * a + __uint_as_float(v[i]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[s]);
+        return true;
+      };
+      float alpha_pending = 1.f;
+      for (int j = 0; ok && j < n_tiles; ++j, ++gt) {
+        const int s = static_cast<int>(gt & 1);
+        const uint32_t ph = static_cast<uint32_t>((gt >> 1) & 1);
+        if (!mbar_wait_warp(&s_full[s], ph, p.status, kTimeoutEpilogue, abort_flag)) {
+          ok = false;
+          break;
         }
-      }
-      red_max[j & 1][half][r] = mx;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&xbar[j & 1]);
-      if (!mbar_wait_warp(&xbar[j & 1], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) {
-        ok = false;
-        break;
-      }
-      mx = fmaxf(mx, red_max[j & 1][half ^ 1][r]);
-      const float m_new = fmaxf(m_cur, mx * p.scale_log2);
-      const float a = exp2f(m_cur - m_new);  // m_cur = -inf on the first tile -> 0
-      const float nm = -m_new;
-      float rsum = 0.f;
-      uint8_t* panel = sP + s * kPBytes + half * (kM * 128);
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const uint32_t(&v)[32] = c == 0 ? v0 : v1;
-        uint32_t pk[16];
+        tc_fence_after();
+        const int valid = min(kN, p.Nk - j * kN) - half * 64;  // valid columns of this half
+        const uint32_t ts = tS + s * kN + lane_off + half * 64;
+        uint32_t v0[32], v1[32];
+        tmem_ld32(ts, v0);
+        tmem_ld32(ts + 32, v1);
+        tmem_wait_ld();
+        const bool full_tile = valid >= 64;
+        float mx = -INFINITY;
         if (full_tile) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            // even columns on the MUFU, odd columns on the FMA pipe (polynomial 2^x)
-            const float e0 = exp2_mufu(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, nm));
-            const float e1 = exp2_poly(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, nm));
-            pk[i] = pack_bf16x2(e0, e1);
-            rsum += e0 + e1;
-          }
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(__uint_as_float(v0[i]), __uint_as_float(v1[i])));
         } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int col = c * 32 + 2 * i;
-            const float e0 = col < valid ? exp2_mufu(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, nm)) : 0.f;
-            const float e1 = col + 1 < valid ? exp2_poly(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, nm)) : 0.f;
-            pk[i] = pack_bf16x2(e0, e1);
-            rsum += e0 + e1;
+          for (int i = 0; i < 32; ++i) {
+            if (i < valid) mx = fmaxf(mx, __uint_as_float(v0[i]));
+            if (32 + i < valid) mx = fmaxf(mx, __uint_as_float(v1[i]));
           }
         }
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int chunk = c * 4 + cc;
-          *reinterpret_cast<uint4*>(panel + r * 128 + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+        red_max[s][half][r] = mx;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xbar[s]);
+        if (!mbar_wait_warp(&xbar[s], ph, p.status, kTimeoutEpilogue, abort_flag)) {
+          ok = false;
+          break;
         }
+        mx = fmaxf(mx, red_max[s][half ^ 1][r]);
+        const float m_new = fmaxf(m_cur, mx * p.scale_log2);
+        const float a = exp2f(m_cur - m_new);  // m_cur = -inf on the first tile -> 0
+        const float nm = -m_new;
+        float rsum = 0.f;
+        uint8_t* panel = sP + s * kPBytes + half * (kM * 128);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t(&v)[32] = c == 0 ? v0 : v1;
+          uint32_t pk[16];
+          if (full_tile) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              // even columns on the MUFU, odd columns on the FMA pipe (polynomial 2^x)
+              const float e0 = exp2_mufu(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, nm));
+              const float e1 = exp2_poly(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, nm));
+              pk[i] = pack_bf16x2(e0, e1);
+              rsum += e0 + e1;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int col = c * 32 + 2 * i;
+              const float e0 = col < valid ? exp2_mufu(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, nm)) : 0.f;
+              const float e1 =
+                  col + 1 < valid ? exp2_poly(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, nm)) : 0.f;
+              pk[i] = pack_bf16x2(e0, e1);
+              rsum += e0 + e1;
+            }
+          }
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int chunk = c * 4 + cc;
+            *reinterpret_cast<uint4*>(panel + r * 128 + ((chunk ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+          }
+        }
+        l = l * a + rsum;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[s]);
+        if (j >= 1 && !absorb(gt - 1, alpha_pending)) {
+          ok = false;
+          break;
+        }
+        alpha_pending = a;
+        m_cur = m_new;
       }
-      l = l * a + rsum;
-      fence_proxy_async_smem();
-      tc_fence_before();
+      if (ok) ok = absorb(gt - 1, alpha_pending);
+      red_sum[it & 1][half][r] = l;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[s]);
-      if (j >= 1 && !absorb(j - 1, alpha_pending)) {
-        ok = false;
-        break;
-      }
-      alpha_pending = a;
-      m_cur = m_new;
-    }
-    if (ok && n_tiles > 0) ok = absorb(n_tiles - 1, alpha_pending);
-    red_sum[half][r] = l;
-    __syncwarp();
-    if (lane == 0) mbar_arrive(sbar);
-    if (ok) ok = mbar_wait_warp(sbar, 0, p.status, kTimeoutEpilogue, abort_flag);
-    if (ok) {
-      const float lt = red_sum[0][r] + red_sum[1][r];
-      const int row = q0 + r;
-      if (row < p.Nq) {
-        const float inv = lt > 0.f ? 1.f / lt : 0.f;
-        __nv_bfloat16* out = p.o + static_cast<int64_t>(i0) * p.o_s0 + static_cast<int64_t>(i1) * p.o_s1 +
-                             static_cast<int64_t>(i2) * p.o_s2 + static_cast<int64_t>(row) * p.o_row + half * 32;
+      if (lane == 0) mbar_arrive(&sbar[it & 1]);
+      if (ok) ok = mbar_wait_warp(&sbar[it & 1], (it >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag);
+      if (ok) {
+        const float lt = red_sum[it & 1][0][r] + red_sum[it & 1][1][r];
+        const int row = q0 + r;
+        if (row < p.Nq) {
+          const float inv = lt > 0.f ? 1.f / lt : 0.f;
+          __nv_bfloat16* out = p.o + static_cast<int64_t>(i0) * p.o_s0 + static_cast<int64_t>(i1) * p.o_s1 +
+                               static_cast<int64_t>(i2) * p.o_s2 + static_cast<int64_t>(row) * p.o_row + half * 32;
 #pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          if (half * 32 + c8 * 8 < p.d_valid) {
-            *reinterpret_cast<uint4*>(out + c8 * 8) =
-                make_uint4(pack_bf16x2(o[c8 * 8] * inv, o[c8 * 8 + 1] * inv),
-                           pack_bf16x2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv),
-                           pack_bf16x2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv),
-                           pack_bf16x2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv));
+          for (int c8 = 0; c8 < 4; ++c8) {
+            if (half * 32 + c8 * 8 < p.d_valid) {
+              *reinterpret_cast<uint4*>(out + c8 * 8) =
+                  make_uint4(pack_bf16x2(o[c8 * 8] * inv, o[c8 * 8 + 1] * inv),
+                             pack_bf16x2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv),
+                             pack_bf16x2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv),
+                             pack_bf16x2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv));
+            }
           }
-        }
-        if (p.lse != nullptr && half == 0) {
-          constexpr float kLn2 = 0.6931471805599453f;
-          p.lse[bh * p.Nq + row] = lt > 0.f ? (m_cur + log2f(lt)) * kLn2 : -INFINITY;
+          if (p.lse != nullptr && half == 0) {
+            constexpr float kLn2 = 0.6931471805599453f;
+            p.lse[bh * p.Nq + row] = lt > 0.f ? (m_cur + log2f(lt)) * kLn2 : -INFINITY;
+          }
         }
       }
     }
@@ -489,10 +556,12 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       constexpr uint32_t id_q = umma_idesc_bf16(kM, kD, true, true);      // dQ: A (dS) MN-major, B (K) MN-major
       const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP), aDS = smem_u32(sDS);
       bool ok = mbar_wait(kv_full, 0, p.status, kTimeoutMma, abort_flag);
-      for (int j = 0; ok && j < n_qt; ++j) {
+      // S^T / dP^T of block j+1 are issued as soon as the softmax warps have read block
+      // j's (s_free), so they run on the tensor core while block j's P / dS are formed
+      auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
-        if (!mbar_wait(&qd_full[s], (j >> 1) & 1, p.status, kTimeoutMma, abort_flag)) break;
-        if (j >= 1 && !mbar_wait(s_free, (j - 1) & 1, p.status, kTimeoutMma, abort_flag)) break;
+        if (!mbar_wait(&qd_full[s], (j >> 1) & 1, p.status, kTimeoutMma, abort_flag)) return false;
+        if (j >= 1 && !mbar_wait(s_free, (j - 1) & 1, p.status, kTimeoutMma, abort_flag)) return false;
         tc_fence_after();
         const uint32_t aQ = smem_u32(sQ + s * kTile), aDO = smem_u32(sDO + s * kTile);
 #pragma unroll
@@ -501,9 +570,16 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
           umma_bf16_ss(tDP, umma_desc_kmajor_sw128(aV + k * 32), umma_desc_kmajor_sw128(aDO + k * 32), id_s, k > 0);
         }
         umma_commit(s_full);
+        return true;
+      };
+      if (ok && n_qt > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < n_qt; ++j) {
+        const int s = j & 1;
+        if (j + 1 < n_qt && !issue_s(j + 1)) break;
         if (!mbar_wait(p_full, j & 1, p.status, kTimeoutMma, abort_flag)) break;
         if (j >= 1 && !mbar_wait(dq_free, (j - 1) & 1, p.status, kTimeoutMma, abort_flag)) break;
         tc_fence_after();
+        const uint32_t aQ = smem_u32(sQ + s * kTile), aDO = smem_u32(sDO + s * kTile);
 #pragma unroll
         for (int k = 0; k < kM / 16; ++k) {
           // K-major A over q: panel (k >> 2), 32-byte steps; MN-major B over q rows: 2048-byte steps
@@ -742,8 +818,11 @@ void attn_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
   }
   TORCH_CHECK(BH <= 2147483647LL, "attn_fwd_tc: too many heads");
   p.n_tiles_q = static_cast<int>((Nq + fa::kM - 1) / fa::kM);
-  TORCH_CHECK(BH * p.n_tiles_q < 2147483647LL, "attention grid too large");
-  dim3 grid(static_cast<unsigned>(BH * p.n_tiles_q));
+  p.n_items = BH * p.n_tiles_q;
+  static int n_sm[64] = {0};
+  if (n_sm[dev] == 0) C10_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev));
+  // persistent: one CTA per SM, each looping over work items
+  dim3 grid(static_cast<unsigned>(std::min<int64_t>(p.n_items, n_sm[dev])));
   attn_fwd_tc_kernel<<<grid, fa::kThreads, fa::kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(mq.map, mk.map, mv.map, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

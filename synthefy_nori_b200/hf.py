@@ -42,8 +42,55 @@ def download_checkpoint(model: str = "nori-6m", filename: str | None = None, cac
         ) from exc
 
 
-def push_checkpoint(path: str, repo_id: str, filename: str = DEFAULT_FILENAME, token=None) -> None:
-    """Upload a checkpoint file to a hub repository (reference ``hf.py:push_checkpoint``)."""
+LIMIX_REPO_ID = "stableai-org/LimiX-2M"
+LIMIX_FILENAME = "LimiX-2M.ckpt"
+
+
+def download_limix(cache_dir: str | None = None, token=None) -> str:
+    """The LimiX-2M base checkpoint (reference ``hf.py:162``)."""
+    return download_checkpoint(LIMIX_REPO_ID, filename=LIMIX_FILENAME, cache_dir=cache_dir, token=token)
+
+
+def push_checkpoint(path: str, repo_id: str, filename: str = DEFAULT_FILENAME, token=None, *, private: bool = True,
+                    create_repo: bool = True, commit_message: str | None = None) -> None:
+    """Upload a checkpoint file to a hub repository (reference ``hf.py:180``)."""
     from huggingface_hub import HfApi
 
-    HfApi(token=token).upload_file(path_or_fileobj=path, path_in_repo=filename, repo_id=repo_id)
+    api = HfApi(token=token)
+    if create_repo:
+        api.create_repo(repo_id, private=private, exist_ok=True, repo_type="model")
+    api.upload_file(path_or_fileobj=path, path_in_repo=filename, repo_id=repo_id, commit_message=commit_message)
+
+
+def download_cli(argv=None) -> int:
+    """``synthefy-nori-b200-download``: fetch a checkpoint and print its local path."""
+    import argparse
+
+    ap = argparse.ArgumentParser(description="Download a Nori checkpoint")
+    src = ap.add_mutually_exclusive_group()
+    src.add_argument("--model", default="nori-6m", help="registry name (" + ", ".join(NORI_MODELS) + ")")
+    src.add_argument("--repo-id", default=None)
+    ap.add_argument("--filename", default=None)
+    ap.add_argument("--cache-dir", default=None)
+    ap.add_argument("--token", default=None)
+    a = ap.parse_args(argv)
+    print(download_checkpoint(a.repo_id or a.model, filename=a.filename, cache_dir=a.cache_dir, token=a.token))
+    return 0
+
+
+def upload_cli(argv=None) -> int:
+    """``synthefy-nori-b200-upload``: push a checkpoint file to a hub repository."""
+    import argparse
+
+    ap = argparse.ArgumentParser(description="Upload a Nori checkpoint")
+    ap.add_argument("checkpoint_path")
+    ap.add_argument("--repo-id", required=True)
+    ap.add_argument("--filename", default=None)
+    ap.add_argument("--public", action="store_true")
+    ap.add_argument("--token", default=None)
+    ap.add_argument("--commit-message", default=None)
+    ap.add_argument("--no-create-repo", action="store_true")
+    a = ap.parse_args(argv)
+    push_checkpoint(a.checkpoint_path, a.repo_id, a.filename or os.path.basename(a.checkpoint_path), a.token,
+                    private=not a.public, create_repo=not a.no_create_repo, commit_message=a.commit_message)
+    return 0
