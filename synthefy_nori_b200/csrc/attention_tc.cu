@@ -413,7 +413,9 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
 }
 
 // ------------------------------------------------------------------ backward
-// One CTA = 128 keys of one head; loop over 128-row query blocks:
+// Persistent: one CTA per SM loops over work items (one item = 128 keys of one head;
+// K / V double-buffered so the next item's load overlaps this one; dK / dV in TMEM are
+// handed back through acc_free).  Per item, loop over 128-row query blocks:
 //   S^T  = K Q^T     (M=128 keys, N=128 q, K=64)   -> TMEM
 //   dP^T = V dO^T    (M=128 keys, N=128 q, K=64)   -> TMEM
 //   softmax warps (thread = key row, two warps per lane quarter split the q columns):
@@ -429,14 +431,15 @@ constexpr int kThreads = 384;  // warps 0 (TMA), 1 (MMA), 4..11 (softmax / drain
 constexpr int kWarpsSm = 8;
 constexpr int kTile = kM * kD * 2;      // 16 KB
 constexpr int kPanel = kM * 128;        // 16 KB: 128 rows x 64 bf16
-// smem: K | V | Q[2] | dO[2] | P^T (2 panels) | dS^T (2 panels) | barriers
-constexpr int kSmemBytes = kTile * 6 + 4 * kPanel + 1024 + 256;
+// smem: K[2] | V[2] | Q[2] | dO[2] | P^T (2 panels) | dS^T (2 panels) | barriers
+constexpr int kSmemBytes = kTile * 8 + 4 * kPanel + 1024 + 256;  // K[2] V[2] Q[2] dO[2] | P, dS panels
 constexpr uint32_t kTmemCols = 512;  // S 0..127, dP 128..255, dV 256..319, dK 320..383, dQ 384..447
 }  // namespace fb
 
 struct AttnBwdTcParams {
   int Nq, Nk, d_valid;
   int n_tiles_k;
+  int64_t n_items;  // BH * n_tiles_k work items (head, key tile), visited with stride gridDim.x
   float scale, scale_log2;
   int q_pos[4], kv_pos[4];
   int d1, d2;
@@ -461,40 +464,39 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
   using namespace fb;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sK = smem;
-  uint8_t* sV = sK + kTile;
-  uint8_t* sQ = sV + kTile;        // 2 stages
+  uint8_t* sK = smem;              // 2 buffers (consecutive work items)
+  uint8_t* sV = sK + 2 * kTile;    // 2 buffers
+  uint8_t* sQ = sV + 2 * kTile;    // 2 stages
   uint8_t* sDO = sQ + 2 * kTile;   // 2 stages
   uint8_t* sP = sDO + 2 * kTile;   // 2 panels
   uint8_t* sDS = sP + 2 * kPanel;  // 2 panels
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDS + 2 * kPanel);
-  uint64_t* kv_full = bars;        // 1
-  uint64_t* qd_full = bars + 1;    // [2]
-  uint64_t* qd_empty = bars + 3;   // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* s_free = bars + 6;
-  uint64_t* p_full = bars + 7;
-  uint64_t* pds_free = bars + 8;
-  uint64_t* dq_full = bars + 9;
-  uint64_t* dq_free = bars + 10;
-  uint64_t* acc_full = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* kv_full = bars;        // [2]
+  uint64_t* kv_empty = bars + 2;   // [2]
+  uint64_t* qd_full = bars + 4;    // [2]
+  uint64_t* qd_empty = bars + 6;   // [2]
+  uint64_t* s_full = bars + 8;
+  uint64_t* s_free = bars + 9;
+  uint64_t* p_full = bars + 10;
+  uint64_t* pds_free = bars + 11;
+  uint64_t* dq_full = bars + 12;
+  uint64_t* dq_free = bars + 13;
+  uint64_t* acc_full = bars + 14;
+  uint64_t* acc_free = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // per-stage query vectors: LSE (log2 units) and Dvec of the block's 128 queries
   __shared__ float s_lse[2][kM], s_dv[2][kM];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int64_t bh = blockIdx.x / p.n_tiles_k;
-  const int k0 = static_cast<int>(blockIdx.x % p.n_tiles_k) * kM;
-  const int i2 = static_cast<int>(bh % p.d2);
-  const int i1 = static_cast<int>((bh / p.d2) % p.d1);
-  const int i0 = static_cast<int>(bh / (static_cast<int64_t>(p.d1) * p.d2));
   const int n_qt = (p.Nq + kM - 1) / kM;
+  const int64_t n_items = p.n_items;
   if (p.status != nullptr && *reinterpret_cast<volatile int*>(p.status) != 0) return;
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
       mbar_init(&qd_full[i], 2);  // TMA (expect_tx) + the producer warp's vector loads
       mbar_init(&qd_empty[i], 1);
     }
@@ -505,6 +507,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
     mbar_init(dq_full, 1);
     mbar_init(dq_free, kWarpsSm);
     mbar_init(acc_full, 1);
+    mbar_init(acc_free, kWarpsSm);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -515,209 +518,253 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
 
+  // work item w -> (head bh, key tile); items are visited with stride gridDim.x
+  auto item_coords = [&](int64_t w, int& k0, int& i2, int& i1, int& i0, int64_t& bh) {
+    bh = w / p.n_tiles_k;
+    k0 = static_cast<int>(w % p.n_tiles_k) * kM;
+    i2 = static_cast<int>(bh % p.d2);
+    i1 = static_cast<int>((bh / p.d2) % p.d1);
+    i0 = static_cast<int>(bh / (static_cast<int64_t>(p.d1) * p.d2));
+  };
+
   if (warp == 0) {
     // whole warp: lane 0 issues the TMA loads, all lanes stage LSE / Dvec of the block
-    const float* lse_g = p.lse + bh * p.Nq;
-    const float* dv_g = p.dvec + bh * p.Nq;
     constexpr float kLog2e = 1.4426950408889634f;
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmDO);
-      int c[5];
-      coords_for(p.kv_pos, k0, i2, i1, i0, c);
-      mbar_arrive_expect_tx(kv_full, 2 * kTile);
-      tma_load_5d(sK, &tmK, kv_full, c);
-      tma_load_5d(sV, &tmV, kv_full, c);
     }
-    for (int j = 0; j < n_qt; ++j) {
-      const int s = j & 1;
-      if (!mbar_wait_warp(&qd_empty[s], ((j >> 1) & 1) ^ 1, p.status, kTimeoutProducer, abort_flag)) break;
+    int64_t gq = 0;  // global query-block counter (Q / dO stages)
+    int it = 0;
+    bool pok = true;
+    for (int64_t w = blockIdx.x; pok && w < n_items; w += gridDim.x, ++it) {
+      int k0, i2, i1, i0;
+      int64_t bh;
+      item_coords(w, k0, i2, i1, i0, bh);
+      const int kb = it & 1;
+      if (!(pok = mbar_wait_warp(&kv_empty[kb], ((it >> 1) & 1) ^ 1, p.status, kTimeoutProducer, abort_flag))) break;
       if (lane == 0) {
         int c[5];
-        coords_for(p.q_pos, j * kM, i2, i1, i0, c);
-        mbar_arrive_expect_tx(&qd_full[s], 2 * kTile);
-        tma_load_5d(sQ + s * kTile, &tmQ, &qd_full[s], c);
-        tma_load_5d(sDO + s * kTile, &tmDO, &qd_full[s], c);
+        coords_for(p.kv_pos, k0, i2, i1, i0, c);
+        mbar_arrive_expect_tx(&kv_full[kb], 2 * kTile);
+        tma_load_5d(sK + kb * kTile, &tmK, &kv_full[kb], c);
+        tma_load_5d(sV + kb * kTile, &tmV, &kv_full[kb], c);
       }
-      for (int i = lane; i < kM; i += 32) {
-        const int qi = j * kM + i;
-        s_lse[s][i] = qi < p.Nq ? lse_g[qi] * kLog2e : INFINITY;
-        s_dv[s][i] = qi < p.Nq ? dv_g[qi] : 0.f;
+      const float* lse_g = p.lse + bh * p.Nq;
+      const float* dv_g = p.dvec + bh * p.Nq;
+      for (int j = 0; j < n_qt; ++j, ++gq) {
+        const int s = static_cast<int>(gq & 1);
+        if (!(pok = mbar_wait_warp(&qd_empty[s], ((gq >> 1) & 1) ^ 1, p.status, kTimeoutProducer, abort_flag))) break;
+        if (lane == 0) {
+          int c[5];
+          coords_for(p.q_pos, j * kM, i2, i1, i0, c);
+          mbar_arrive_expect_tx(&qd_full[s], 2 * kTile);
+          tma_load_5d(sQ + s * kTile, &tmQ, &qd_full[s], c);
+          tma_load_5d(sDO + s * kTile, &tmDO, &qd_full[s], c);
+        }
+        for (int i = lane; i < kM; i += 32) {
+          const int qi = j * kM + i;
+          s_lse[s][i] = qi < p.Nq ? lse_g[qi] * kLog2e : INFINITY;
+          s_dv[s][i] = qi < p.Nq ? dv_g[qi] : 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&qd_full[s]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&qd_full[s]);
     }
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t id_s = umma_idesc_bf16(kM, kM, false, false);    // S^T, dP^T
       constexpr uint32_t id_kv = umma_idesc_bf16(kM, kD, false, true);    // dV, dK: A K-major, B MN-major
       constexpr uint32_t id_q = umma_idesc_bf16(kM, kD, true, true);      // dQ: A (dS) MN-major, B (K) MN-major
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP), aDS = smem_u32(sDS);
-      bool ok = mbar_wait(kv_full, 0, p.status, kTimeoutMma, abort_flag);
-      // S^T / dP^T of block j+1 are issued as soon as the softmax warps have read block
-      // j's (s_free), so they run on the tensor core while block j's P / dS are formed
-      auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&qd_full[s], (j >> 1) & 1, p.status, kTimeoutMma, abort_flag)) return false;
-        if (j >= 1 && !mbar_wait(s_free, (j - 1) & 1, p.status, kTimeoutMma, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t aQ = smem_u32(sQ + s * kTile), aDO = smem_u32(sDO + s * kTile);
+      const uint32_t aP = smem_u32(sP), aDS = smem_u32(sDS);
+      int64_t gq = 0;  // global query-block counter: Q / dO stage and the S / P / dQ barrier phases
+      int it = 0;
+      bool ok = true;
+      for (int64_t w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
+        const int kb = it & 1;
+        const uint32_t aK = smem_u32(sK + kb * kTile), aV = smem_u32(sV + kb * kTile);
+        if (!(ok = mbar_wait(&kv_full[kb], (it >> 1) & 1, p.status, kTimeoutMma, abort_flag))) break;
+        // S^T / dP^T of block g+1 are issued as soon as the softmax warps have read block
+        // g's (s_free), so they run on the tensor core while block g's P / dS are formed
+        auto issue_s = [&](int64_t g) -> bool {
+          const int s = static_cast<int>(g & 1);
+          if (!mbar_wait(&qd_full[s], (g >> 1) & 1, p.status, kTimeoutMma, abort_flag)) return false;
+          if (g >= 1 && !mbar_wait(s_free, (g - 1) & 1, p.status, kTimeoutMma, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t aQ = smem_u32(sQ + s * kTile), aDO = smem_u32(sDO + s * kTile);
 #pragma unroll
-        for (int k = 0; k < kD / 16; ++k) {
-          umma_bf16_ss(tS, umma_desc_kmajor_sw128(aK + k * 32), umma_desc_kmajor_sw128(aQ + k * 32), id_s, k > 0);
-          umma_bf16_ss(tDP, umma_desc_kmajor_sw128(aV + k * 32), umma_desc_kmajor_sw128(aDO + k * 32), id_s, k > 0);
-        }
-        umma_commit(s_full);
-        return true;
-      };
-      if (ok && n_qt > 0) ok = issue_s(0);
-      for (int j = 0; ok && j < n_qt; ++j) {
-        const int s = j & 1;
-        if (j + 1 < n_qt && !issue_s(j + 1)) break;
-        if (!mbar_wait(p_full, j & 1, p.status, kTimeoutMma, abort_flag)) break;
-        if (j >= 1 && !mbar_wait(dq_free, (j - 1) & 1, p.status, kTimeoutMma, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t aQ = smem_u32(sQ + s * kTile), aDO = smem_u32(sDO + s * kTile);
+          for (int k = 0; k < kD / 16; ++k) {
+            umma_bf16_ss(tS, umma_desc_kmajor_sw128(aK + k * 32), umma_desc_kmajor_sw128(aQ + k * 32), id_s, k > 0);
+            umma_bf16_ss(tDP, umma_desc_kmajor_sw128(aV + k * 32), umma_desc_kmajor_sw128(aDO + k * 32), id_s, k > 0);
+          }
+          umma_commit(s_full);
+          return true;
+        };
+        if (!(ok = issue_s(gq))) break;
+        // the previous item's dK / dV must have been read before block 0 overwrites them
+        if (it >= 1 && !(ok = mbar_wait(acc_free, (it - 1) & 1, p.status, kTimeoutMma, abort_flag))) break;
+        for (int j = 0; ok && j < n_qt; ++j, ++gq) {
+          const int s = static_cast<int>(gq & 1);
+          if (j + 1 < n_qt && !(ok = issue_s(gq + 1))) break;
+          if (!(ok = mbar_wait(p_full, gq & 1, p.status, kTimeoutMma, abort_flag))) break;
+          if (gq >= 1 && !(ok = mbar_wait(dq_free, (gq - 1) & 1, p.status, kTimeoutMma, abort_flag))) break;
+          tc_fence_after();
+          const uint32_t aQ = smem_u32(sQ + s * kTile), aDO = smem_u32(sDO + s * kTile);
 #pragma unroll
-        for (int k = 0; k < kM / 16; ++k) {
-          // K-major A over q: panel (k >> 2), 32-byte steps; MN-major B over q rows: 2048-byte steps
-          const uint64_t dP = umma_desc_kmajor_sw128(aP + (k >> 2) * kPanel + (k & 3) * 32);
-          const uint64_t dS = umma_desc_kmajor_sw128(aDS + (k >> 2) * kPanel + (k & 3) * 32);
-          umma_bf16_ss(tDV, dP, umma_smem_desc(aDO + k * 2048, 8192, 1024, 2), id_kv, (j > 0 || k > 0));
-          umma_bf16_ss(tDK, dS, umma_smem_desc(aQ + k * 2048, 8192, 1024, 2), id_kv, (j > 0 || k > 0));
-        }
+          for (int k = 0; k < kM / 16; ++k) {
+            // K-major A over q: panel (k >> 2), 32-byte steps; MN-major B over q rows: 2048-byte steps
+            const uint64_t dP = umma_desc_kmajor_sw128(aP + (k >> 2) * kPanel + (k & 3) * 32);
+            const uint64_t dS = umma_desc_kmajor_sw128(aDS + (k >> 2) * kPanel + (k & 3) * 32);
+            umma_bf16_ss(tDV, dP, umma_smem_desc(aDO + k * 2048, 8192, 1024, 2), id_kv, (j > 0 || k > 0));
+            umma_bf16_ss(tDK, dS, umma_smem_desc(aQ + k * 2048, 8192, 1024, 2), id_kv, (j > 0 || k > 0));
+          }
 #pragma unroll
-        for (int k = 0; k < kM / 16; ++k) {
-          // A = dS [q x keys] read MN-major from dS^T (rows = keys): 16 key rows per step
-          const uint64_t da = umma_smem_desc(aDS + k * 2048, kPanel, 1024, 2);
-          const uint64_t db = umma_smem_desc(aK + k * 2048, 8192, 1024, 2);
-          umma_bf16_ss(tDQ, da, db, id_q, k > 0);
+          for (int k = 0; k < kM / 16; ++k) {
+            // A = dS [q x keys] read MN-major from dS^T (rows = keys): 16 key rows per step
+            const uint64_t da = umma_smem_desc(aDS + k * 2048, kPanel, 1024, 2);
+            const uint64_t db = umma_smem_desc(aK + k * 2048, 8192, 1024, 2);
+            umma_bf16_ss(tDQ, da, db, id_q, k > 0);
+          }
+          umma_commit(pds_free);
+          umma_commit(dq_full);
+          umma_commit(&qd_empty[s]);
         }
-        umma_commit(pds_free);
-        umma_commit(dq_full);
-        umma_commit(&qd_empty[s]);
+        if (ok) {
+          umma_commit(acc_full);
+          umma_commit(&kv_empty[kb]);
+        }
       }
-      if (ok) umma_commit(acc_full);
     }
   } else if (warp >= 4) {
     const int q4 = warp & 3;
     const int half = (warp - 4) >> 2;
     const int r = q4 * 32 + lane;  // TMEM lane: key row for S/dP/dK/dV, query row for dQ
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    const int key = k0 + r;
-    const bool key_ok = key < p.Nk;
-    float* dq_b = p.dq + static_cast<int64_t>(i0) * p.dq_s0 + static_cast<int64_t>(i1) * p.dq_s1 +
-                  static_cast<int64_t>(i2) * p.dq_s2;
     bool ok = true;
-    auto drain_dq = [&](int jj) -> bool {
-      if (!mbar_wait_warp(dq_full, jj & 1, p.status, kTimeoutEpilogue, abort_flag)) return false;
-      tc_fence_after();
-      uint32_t v[32];
-      tmem_ld32(tDQ + lane_off + half * 32, v);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
-      const int qrow = jj * kM + r;
-      if (qrow < p.Nq) {
-        float* dst = dq_b + static_cast<int64_t>(qrow) * p.dq_row + half * 32;
+    int64_t gq = 0;
+    int it = 0;
+    for (int64_t w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
+      int k0, i2, i1, i0;
+      int64_t bh;
+      item_coords(w, k0, i2, i1, i0, bh);
+      const int key = k0 + r;
+      const bool key_ok = key < p.Nk;
+      float* dq_b = p.dq + static_cast<int64_t>(i0) * p.dq_s0 + static_cast<int64_t>(i1) * p.dq_s1 +
+                    static_cast<int64_t>(i2) * p.dq_s2;
+      auto drain_dq = [&](int64_t g, int jj) -> bool {
+        if (!mbar_wait_warp(dq_full, g & 1, p.status, kTimeoutEpilogue, abort_flag)) return false;
+        tc_fence_after();
+        uint32_t v[32];
+        tmem_ld32(tDQ + lane_off + half * 32, v);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_free);
+        const int qrow = jj * kM + r;
+        if (qrow < p.Nq) {
+          float* dst = dq_b + static_cast<int64_t>(qrow) * p.dq_row + half * 32;
 #pragma unroll
-        for (int i = 0; i < 32; i += 2)
-          if (half * 32 + i < p.d_valid) red_add_v2(dst + i, __uint_as_float(v[i]) * p.scale, __uint_as_float(v[i + 1]) * p.scale);
-      }
-      return true;
-    };
-    for (int j = 0; ok && j < n_qt; ++j) {
-      if (!mbar_wait_warp(s_full, j & 1, p.status, kTimeoutEpilogue, abort_flag)) {
-        ok = false;
-        break;
-      }
-      // the block's LSE / Dvec were staged before qd_full completed (acquire it here too)
-      if (!mbar_wait_warp(&qd_full[j & 1], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const float* sl = s_lse[j & 1] + half * 64;
-      const float* sd = s_dv[j & 1] + half * 64;
-      uint32_t sv[64], dp[64];
-      tmem_ld32(tS + lane_off + half * 64, *reinterpret_cast<uint32_t(*)[32]>(sv));
-      tmem_ld32(tS + lane_off + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-      tmem_ld32(tDP + lane_off + half * 64, *reinterpret_cast<uint32_t(*)[32]>(dp));
-      tmem_ld32(tDP + lane_off + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dp + 32));
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);
-      // P and dS of the previous block must have been consumed before we overwrite them
-      if (j >= 1 && !mbar_wait_warp(pds_free, (j - 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) {
-        ok = false;
-        break;
-      }
-      const int qbase = j * kM + half * 64;
-      uint8_t* panelP = sP + half * kPanel;
-      uint8_t* panelS = sDS + half * kPanel;
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        uint32_t pk[4], dk4[4];
-#pragma unroll
-        for (int i2p = 0; i2p < 4; ++i2p) {
-          float pe[2], de[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int col = ch * 8 + i2p * 2 + e;
-            const int qi = qbase + col;
-            float pv = 0.f, ds = 0.f;
-            if (key_ok && qi < p.Nq) {
-              pv = exp2_mufu(fmaf(__uint_as_float(sv[col]), p.scale_log2, -sl[col]));
-              ds = pv * (__uint_as_float(dp[col]) - sd[col]);
-            }
-            pe[e] = pv;
-            de[e] = ds;
-          }
-          pk[i2p] = pack_bf16x2(pe[0], pe[1]);
-          dk4[i2p] = pack_bf16x2(de[0], de[1]);
+          for (int i = 0; i < 32; i += 2)
+            if (half * 32 + i < p.d_valid)
+              red_add_v2(dst + i, __uint_as_float(v[i]) * p.scale, __uint_as_float(v[i + 1]) * p.scale);
         }
-        *reinterpret_cast<uint4*>(panelP + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(panelS + r * 128 + ((ch ^ (r & 7)) << 4)) =
-            make_uint4(dk4[0], dk4[1], dk4[2], dk4[3]);
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      if (j >= 1 && !drain_dq(j - 1)) {
-        ok = false;
-        break;
-      }
-    }
-    if (ok && n_qt > 0) ok = drain_dq(n_qt - 1);
-    if (ok) ok = mbar_wait_warp(acc_full, 0, p.status, kTimeoutEpilogue, abort_flag);
-    if (ok) {
-      tc_fence_after();
-      uint32_t v[32], w[32];
-      tmem_ld32(tDK + lane_off + half * 32, v);
-      tmem_ld32(tDV + lane_off + half * 32, w);
-      tmem_wait_ld();
-      if (key_ok) {
-        const int64_t off = static_cast<int64_t>(i0) * p.kv_s0 + static_cast<int64_t>(i1) * p.kv_s1 +
-                            static_cast<int64_t>(i2) * p.kv_s2 + static_cast<int64_t>(key) * p.kv_row + half * 32;
+        return true;
+      };
+      for (int j = 0; ok && j < n_qt; ++j, ++gq) {
+        if (!mbar_wait_warp(s_full, gq & 1, p.status, kTimeoutEpilogue, abort_flag)) {
+          ok = false;
+          break;
+        }
+        // the block's LSE / Dvec were staged before qd_full completed (acquire it here too)
+        if (!mbar_wait_warp(&qd_full[gq & 1], (gq >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float* sl = s_lse[gq & 1] + half * 64;
+        const float* sd = s_dv[gq & 1] + half * 64;
+        uint32_t sv[64], dp[64];
+        tmem_ld32(tS + lane_off + half * 64, *reinterpret_cast<uint32_t(*)[32]>(sv));
+        tmem_ld32(tS + lane_off + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        tmem_ld32(tDP + lane_off + half * 64, *reinterpret_cast<uint32_t(*)[32]>(dp));
+        tmem_ld32(tDP + lane_off + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dp + 32));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_free);
+        // P and dS of the previous block must have been consumed before we overwrite them
+        if (gq >= 1 && !mbar_wait_warp(pds_free, (gq - 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int qbase = j * kM + half * 64;
+        uint8_t* panelP = sP + half * kPanel;
+        uint8_t* panelS = sDS + half * kPanel;
 #pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          if (half * 32 + c8 * 8 >= p.d_valid) continue;
-          uint4 a, b;
-          a.x = pack_bf16x2(__uint_as_float(v[c8 * 8]) * p.scale, __uint_as_float(v[c8 * 8 + 1]) * p.scale);
-          a.y = pack_bf16x2(__uint_as_float(v[c8 * 8 + 2]) * p.scale, __uint_as_float(v[c8 * 8 + 3]) * p.scale);
-          a.z = pack_bf16x2(__uint_as_float(v[c8 * 8 + 4]) * p.scale, __uint_as_float(v[c8 * 8 + 5]) * p.scale);
-          a.w = pack_bf16x2(__uint_as_float(v[c8 * 8 + 6]) * p.scale, __uint_as_float(v[c8 * 8 + 7]) * p.scale);
-          b.x = pack_bf16x2(__uint_as_float(w[c8 * 8]), __uint_as_float(w[c8 * 8 + 1]));
-          b.y = pack_bf16x2(__uint_as_float(w[c8 * 8 + 2]), __uint_as_float(w[c8 * 8 + 3]));
-          b.z = pack_bf16x2(__uint_as_float(w[c8 * 8 + 4]), __uint_as_float(w[c8 * 8 + 5]));
-          b.w = pack_bf16x2(__uint_as_float(w[c8 * 8 + 6]), __uint_as_float(w[c8 * 8 + 7]));
-          *reinterpret_cast<uint4*>(p.dk + off + c8 * 8) = a;
-          *reinterpret_cast<uint4*>(p.dv + off + c8 * 8) = b;
+        for (int ch = 0; ch < 8; ++ch) {
+          uint32_t pk[4], dk4[4];
+#pragma unroll
+          for (int i2p = 0; i2p < 4; ++i2p) {
+            float pe[2], de[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int col = ch * 8 + i2p * 2 + e;
+              const int qi = qbase + col;
+              float pv = 0.f, ds = 0.f;
+              if (key_ok && qi < p.Nq) {
+                pv = exp2_mufu(fmaf(__uint_as_float(sv[col]), p.scale_log2, -sl[col]));
+                ds = pv * (__uint_as_float(dp[col]) - sd[col]);
+              }
+              pe[e] = pv;
+              de[e] = ds;
+            }
+            pk[i2p] = pack_bf16x2(pe[0], pe[1]);
+            dk4[i2p] = pack_bf16x2(de[0], de[1]);
+          }
+          *reinterpret_cast<uint4*>(panelP + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(panelS + r * 128 + ((ch ^ (r & 7)) << 4)) =
+              make_uint4(dk4[0], dk4[1], dk4[2], dk4[3]);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+        if (j >= 1 && !drain_dq(gq - 1, j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok) ok = drain_dq(gq - 1, n_qt - 1);
+      if (ok) ok = mbar_wait_warp(acc_full, it & 1, p.status, kTimeoutEpilogue, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        uint32_t v[32], wv[32];
+        tmem_ld32(tDK + lane_off + half * 32, v);
+        tmem_ld32(tDV + lane_off + half * 32, wv);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_free);  // the next item may overwrite dK / dV
+        if (key_ok) {
+          const int64_t off = static_cast<int64_t>(i0) * p.kv_s0 + static_cast<int64_t>(i1) * p.kv_s1 +
+                              static_cast<int64_t>(i2) * p.kv_s2 + static_cast<int64_t>(key) * p.kv_row + half * 32;
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            if (half * 32 + c8 * 8 >= p.d_valid) continue;
+            uint4 a, b;
+            a.x = pack_bf16x2(__uint_as_float(v[c8 * 8]) * p.scale, __uint_as_float(v[c8 * 8 + 1]) * p.scale);
+            a.y = pack_bf16x2(__uint_as_float(v[c8 * 8 + 2]) * p.scale, __uint_as_float(v[c8 * 8 + 3]) * p.scale);
+            a.z = pack_bf16x2(__uint_as_float(v[c8 * 8 + 4]) * p.scale, __uint_as_float(v[c8 * 8 + 5]) * p.scale);
+            a.w = pack_bf16x2(__uint_as_float(v[c8 * 8 + 6]) * p.scale, __uint_as_float(v[c8 * 8 + 7]) * p.scale);
+            b.x = pack_bf16x2(__uint_as_float(wv[c8 * 8]), __uint_as_float(wv[c8 * 8 + 1]));
+            b.y = pack_bf16x2(__uint_as_float(wv[c8 * 8 + 2]), __uint_as_float(wv[c8 * 8 + 3]));
+            b.z = pack_bf16x2(__uint_as_float(wv[c8 * 8 + 4]), __uint_as_float(wv[c8 * 8 + 5]));
+            b.w = pack_bf16x2(__uint_as_float(wv[c8 * 8 + 6]), __uint_as_float(wv[c8 * 8 + 7]));
+            *reinterpret_cast<uint4*>(p.dk + off + c8 * 8) = a;
+            *reinterpret_cast<uint4*>(p.dv + off + c8 * 8) = b;
+          }
         }
       }
     }
@@ -883,8 +930,11 @@ void attn_bwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
     C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fb::kSmemBytes));
     configured[dev] = true;
   }
-  TORCH_CHECK(BH * p.n_tiles_k < 2147483647LL, "attention grid too large");
-  attn_bwd_tc_kernel<<<static_cast<unsigned>(BH * p.n_tiles_k), fb::kThreads, fb::kSmemBytes,
+  p.n_items = BH * p.n_tiles_k;
+  static int n_sm[64] = {0};
+  if (n_sm[dev] == 0) C10_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev));
+  // persistent: one CTA per SM, each looping over (head, key tile) work items
+  attn_bwd_tc_kernel<<<static_cast<unsigned>(std::min<int64_t>(p.n_items, n_sm[dev])), fb::kThreads, fb::kSmemBytes,
                        at::cuda::getCurrentCUDAStream()>>>(mq.map, mk.map, mv.map, mdo.map, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

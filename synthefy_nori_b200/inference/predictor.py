@@ -99,7 +99,8 @@ def _tensor(a, device) -> torch.Tensor:
 class NoriPredictor:
     def __init__(self, model, device: torch.device | str | None = None, *, inference_config=None,
                  n_estimators: int | None = None, cache_dtype: str = "bf16", query_chunk_size: int | None = None,
-                 seed: int = 0, reuse_context_cache: bool = True, context_cache_budget_bytes: int | None = None):
+                 seed: int = 0, reuse_context_cache: bool = True, context_cache_budget_bytes: int | None = None,
+                 cuda_graphs: bool = False, graph_rows: int = 1024):
         if device is None:
             device = "cuda" if torch.cuda.is_available() else "cpu"
         self.device = torch.device(device)
@@ -119,6 +120,8 @@ class NoriPredictor:
             context_cache_budget_bytes = (torch.cuda.get_device_properties(self.device).total_memory // 4
                                           if self.device.type == "cuda" else 8 << 30)
         self.store = ContextStore(context_cache_budget_bytes) if reuse_context_cache else None
+        self.cuda_graphs = bool(cuda_graphs) and self.device.type == "cuda"
+        self.graph_rows = int(graph_rows)
 
     # ------------------------------------------------------------------ context
     def _members(self) -> list[MemberPipeline]:
@@ -168,6 +171,16 @@ class NoriPredictor:
         outs = []
         for g in ctx.groups:
             xq = torch.stack([m.transform(X) for m in g.members], 0)
+            if self.cuda_graphs and not return_hidden:
+                runner = getattr(g, "graph_runner", None)
+                if runner is None:
+                    from synthefy_nori_b200.inference.cuda_graphs import GraphedQueryRunner
+
+                    runner = GraphedQueryRunner(self.model, g.cache, xq.shape[0], self.graph_rows, xq.shape[2],
+                                                self.device)
+                    g.graph_runner = runner
+                outs.append(runner(xq).float())
+                continue
             outs.append(self.model.apply_context_cache(xq, g.cache, row_chunk_size=self.query_chunk_size,
                                                        return_hidden=return_hidden).float())
         if return_hidden:

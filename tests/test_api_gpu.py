@@ -57,3 +57,23 @@ def test_default_ensemble_cuda_matches_cpu():
     assert np.max(np.abs(a - b)) < 0.05 * np.std(y) + 1e-3
     e = gpu.get_embeddings(X[240:])
     assert e.shape[:2] == (8, 60) and np.all(np.isfinite(e))
+
+
+def test_cuda_graph_replay_matches_eager():
+    from synthefy_nori_b200.inference.predictor import NoriPredictor
+    from synthefy_nori_b200.models.config import preset_config
+    from synthefy_nori_b200.utils.loading import build_model
+
+    torch.manual_seed(0)
+    model = build_model(preset_config("nori-6m")).cuda().eval()
+    rng = np.random.default_rng(2)
+    X = rng.standard_normal((900, 12)).astype(np.float32)
+    y = X[:, 0] - X[:, 1] ** 2
+    eager = NoriPredictor(model, "cuda", n_estimators=2)
+    graphed = NoriPredictor(model, "cuda", n_estimators=2, cuda_graphs=True, graph_rows=128)
+    ce, cg = eager.fit_context(X[:600], y[:600]), graphed.fit_context(X[:600], y[:600])
+    a = eager.predict_raw(ce, X[600:])
+    b = graphed.predict_raw(cg, X[600:])  # 300 rows: two full chunks and a padded one
+    torch.testing.assert_close(b, a, atol=2e-3, rtol=2e-3)
+    b2 = graphed.predict_raw(cg, X[600:700])  # replay
+    torch.testing.assert_close(b2, a[:100], atol=2e-3, rtol=2e-3)
