@@ -64,7 +64,7 @@ def parse():
     ap.add_argument("--grad-reduction", default="peer", choices=["nccl", "peer"],
                     help="N > 1: peer = in-kernel reduce-scatter / sharded AdamW / all-gather over NVLink peer memory; "
                          "nccl = all-reduce baseline")
-    ap.add_argument("--workload", default="train", choices=["train", "infer5", "infer4"],
+    ap.add_argument("--workload", default="train", choices=["train", "infer5", "infer4", "infer1"],
                     help="train (headline), infer5 (batched multi-table cached inference, BASELINE config 5), "
                          "infer4 (100k-row context, int8 KV, BASELINE config 4)")
     ap.add_argument("--infer-tables", type=int, default=256)
@@ -431,6 +431,58 @@ def run_infer4(args, device, world, rank, impl):
             "context_sharding": f"rows over {world} GPUs" if world > 1 else "none"}
 
 
+def run_infer1(args, impl):
+    """nori-6m single-table inference on the CPU (512 context rows x 10
+    features, 5% NaN, y = Xw + 0.5 sin(3 x0) + N(0, 0.1^2); 128 query rows; the mean plus
+    quantiles 0.1 / 0.5 / 0.9).  Wall-clock latency per call (the CPU has no device timer),
+    median over the timed calls, one model forward per call (no ensemble)."""
+    import numpy as np
+
+    torch.set_num_threads(int(os.environ.get("NORI_CPU_THREADS", "8")))
+    rng = np.random.default_rng(args.seed)
+    X = rng.standard_normal((640, 10)).astype(np.float32)
+    X[rng.random(X.shape) < 0.05] = np.nan
+    w = rng.standard_normal(10)
+    y = (np.nan_to_num(X) @ w + 0.5 * np.sin(3 * np.nan_to_num(X[:, 0])) + 0.1 * rng.standard_normal(640))
+    from synthefy_nori_b200.models.config import preset_config
+
+    if impl == "reference":
+        from synthefy_nori_b200.utils.reference import import_reference
+
+        import_reference()
+        from synthefy_nori.utils.loading import build_model as mk
+    else:
+        from synthefy_nori_b200.utils.loading import build_model as mk
+    torch.manual_seed(args.seed)
+    model = mk(dict(preset_config("nori-6m"))).eval()
+    taus = torch.tensor(model.regression_quantiles, dtype=torch.float64)
+    xt = torch.from_numpy(X).unsqueeze(0)
+    ym, ys = y[:512].mean(), y[:512].std()
+    yt = torch.from_numpy(((y - ym) / ys).astype(np.float32)).unsqueeze(0)
+
+    def call():
+        with torch.no_grad():
+            out = model(xt, yt[:, :512], eval_pos=512, task_type="reg")
+            raw = (out["reg_output"] if isinstance(out, dict) else out)[0].double()
+            q = raw.sort(-1).values
+            mean = taus[0] * q[:, 0] + (1 - taus[-1]) * q[:, -1] + (0.5 * (q[:, 1:] + q[:, :-1]) * taus.diff()).sum(-1)
+            idx = torch.searchsorted(taus, torch.tensor([0.1, 0.5, 0.9], dtype=torch.float64)).clamp(max=len(taus) - 1)
+            return mean * ys + ym, q[:, idx] * ys + ym
+
+    for _ in range(max(args.warmup, 1)):
+        call()
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        call()
+        ts.append((time.perf_counter() - t0) * 1e3)
+    med = float(np.median(ts))
+    return {"metric": "nori-6m single-table CPU inference latency", "value": med, "unit": "ms",
+            "higher_is_better": False, "steps": args.steps, "warmup": args.warmup, "ms_all": [round(t, 2) for t in ts],
+            "cpu_threads": torch.get_num_threads(), "dtype": "fp32", "data": "synthetic (config 1)",
+            "config": {"model": "nori-6m", "ctx_rows": 512, "query_rows": 128, "features": 10, "device": "cpu"}}
+
+
 def main_infer(args, device, world, rank):
     res = run_infer5(args, device, world, rank, args.impl) if args.workload == "infer5" else \
         run_infer4(args, device, world, rank, args.impl)
@@ -445,6 +497,12 @@ def main_infer(args, device, world, rank):
 
 def main():
     args = parse()
+    if args.workload == "infer1":
+        res = run_infer1(args, args.impl)
+        if args.impl == "reference":
+            res["impl"] = "reference"
+        print(json.dumps(res), flush=True)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
