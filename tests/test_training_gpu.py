@@ -38,3 +38,21 @@ def test_loss_spike_skip_leaves_weights():
     y[:, b.eval_pos:] *= 1e3  # a spike
     tr.train_step(b.x, y, b.eval_pos)
     assert tr.skipped_steps == 1 and torch.equal(before, tr.flat.data)
+
+
+def test_mask_prediction_training():
+    from synthefy_nori_b200.models.config import preset_config
+    from synthefy_nori_b200.training.prior import PriorConfig, scm_prior_batch
+    from synthefy_nori_b200.training.trainer import NoriTrainer, TrainConfig
+    from synthefy_nori_b200.utils.loading import build_model
+
+    cfg = preset_config("nori-tiny")
+    cfg["mask_prediction"] = True
+    torch.manual_seed(0)
+    m = build_model(cfg).cuda()
+    assert m.feature_decoder is not None
+    tr = NoriTrainer(m, TrainConfig(lr=1e-3, mask_prediction=True), torch.device("cuda"))
+    b = scm_prior_batch(PriorConfig(max_features=10, pad_features=10), 4, 128, 96, seed=5, device=torch.device("cuda"))
+    losses = [tr.train_step(b.x, b.y, b.eval_pos).item() for _ in range(10)]
+    assert all(torch.isfinite(torch.tensor(losses))) and losses[-1] < losses[0]
+    assert m.feature_decoder[0].weight.grad is not None and m.feature_decoder[0].weight.grad.abs().sum() > 0
