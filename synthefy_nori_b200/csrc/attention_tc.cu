@@ -308,8 +308,13 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         const bool full_tile = valid >= 64;
         float mx = -INFINITY;
         if (full_tile) {
+          // tree reduction: eight independent chains instead of one 64-long dependency chain
+          float m8[8];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(__uint_as_float(v0[i]), __uint_as_float(v1[i])));
+          for (int i = 0; i < 8; ++i) m8[i] = fmaxf(__uint_as_float(v0[i]), __uint_as_float(v1[i]));
+#pragma unroll
+          for (int i = 8; i < 32; ++i) m8[i & 7] = fmaxf(m8[i & 7], fmaxf(__uint_as_float(v0[i]), __uint_as_float(v1[i])));
+          mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
@@ -328,7 +333,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         const float m_new = fmaxf(m_cur, mx * p.scale_log2);
         const float a = exp2f(m_cur - m_new);  // m_cur = -inf on the first tile -> 0
         const float nm = -m_new;
-        float rsum = 0.f;
+        float rs[4] = {0.f, 0.f, 0.f, 0.f};  // four partial row sums (short dependency chains)
         uint8_t* panel = sP + s * kPBytes + half * (kM * 128);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
@@ -341,7 +346,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
               const float e0 = exp2_mufu(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, nm));
               const float e1 = exp2_poly(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, nm));
               pk[i] = pack_bf16x2(e0, e1);
-              rsum += e0 + e1;
+              rs[i & 3] += e0 + e1;
             }
           } else {
 #pragma unroll
@@ -351,7 +356,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
               const float e1 =
                   col + 1 < valid ? exp2_poly(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, nm)) : 0.f;
               pk[i] = pack_bf16x2(e0, e1);
-              rsum += e0 + e1;
+              rs[i & 3] += e0 + e1;
             }
           }
 #pragma unroll
@@ -361,7 +366,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
                 make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
           }
         }
-        l = l * a + rsum;
+        l = l * a + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
