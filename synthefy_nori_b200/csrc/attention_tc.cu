@@ -419,8 +419,8 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
 
 // ------------------------------------------------------------------ backward
 // Persistent: one CTA per SM loops over work items (one item = 128 keys of one head;
-// K / V double-buffered so the next item's load overlaps this one; dK / dV in TMEM are
-// handed back through acc_free).  Per item, loop over 128-row query blocks:
+// dK / dV in TMEM are handed back through acc_free).  Per item, loop over 128-row query
+// blocks:
 //   S^T  = K Q^T     (M=128 keys, N=128 q, K=64)   -> TMEM
 //   dP^T = V dO^T    (M=128 keys, N=128 q, K=64)   -> TMEM
 //   softmax warps (thread = key row, two warps per lane quarter split the q columns):
@@ -428,16 +428,18 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
 //   dV += P^T dO     (M=128 keys, N=64, K=128 q; dO read MN-major)
 //   dK += dS^T Q     (M=128 keys, N=64, K=128 q; Q read MN-major)
 //   dQ  = dS K       (M=128 q, N=64, K=128 keys; dS^T read MN-major as A, K MN-major)
-//   the softmax warps drain dQ (thread = query row) with vector fp32 reductions into
-//   the caller's zeroed accumulator, and finally write dK (scaled) and dV.
+//   the softmax warps drain dQ (thread = query row) into a 4 KB shared-memory slot per
+//   warp and add it to the caller's zeroed fp32 accumulator with one TMA tensor
+//   reduce-add per warp (the additions happen in L2), and finally write dK (scaled) and dV.
 namespace fb {
 constexpr int kM = 128, kD = 64;
 constexpr int kThreads = 384;  // warps 0 (TMA), 1 (MMA), 4..11 (softmax / drain)
 constexpr int kWarpsSm = 8;
 constexpr int kTile = kM * kD * 2;      // 16 KB
 constexpr int kPanel = kM * 128;        // 16 KB: 128 rows x 64 bf16
-// smem: K[2] | V[2] | Q[2] | dO[2] | P^T (2 panels) | dS^T (2 panels) | barriers
-constexpr int kSmemBytes = kTile * 8 + 4 * kPanel + 1024 + 256;  // K[2] V[2] Q[2] dO[2] | P, dS panels
+// smem: K | V | Q[2] | dO[2] | P^T (2 panels) | dS^T (2 panels) | dQ staging (8 x 4 KB) | barriers
+constexpr int kDQStage = 32 * 128;      // 4 KB per drain warp: 32 query rows x 32 fp32 (128B-swizzled)
+constexpr int kSmemBytes = kTile * 6 + 4 * kPanel + kWarpsSm * kDQStage + 1024 + 256;
 constexpr uint32_t kTmemCols = 512;  // S 0..127, dP 128..255, dV 256..319, dK 320..383, dQ 384..447
 }  // namespace fb
 
@@ -446,7 +448,7 @@ struct AttnBwdTcParams {
   int n_tiles_k;
   int64_t n_items;  // BH * n_tiles_k work items (head, key tile), visited with stride gridDim.x
   float scale, scale_log2;
-  int q_pos[4], kv_pos[4];
+  int q_pos[4], kv_pos[4], dq_pos[4];
   int d1, d2;
   const float* lse;   // [BH, Nq]
   const float* dvec;  // [BH, Nq]
@@ -458,26 +460,24 @@ struct AttnBwdTcParams {
   int* status;
 };
 
-__device__ __forceinline__ void red_add_v2(float* addr, float a, float b) {
-  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(addr), "f"(a), "f"(b) : "memory");
-}
 
 __global__ void __launch_bounds__(fb::kThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                       AttnBwdTcParams p) {
+                       const __grid_constant__ CUtensorMap tmDQ, AttnBwdTcParams p) {
   using namespace fb;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sK = smem;              // 2 buffers (consecutive work items)
-  uint8_t* sV = sK + 2 * kTile;    // 2 buffers
-  uint8_t* sQ = sV + 2 * kTile;    // 2 stages
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + kTile;
+  uint8_t* sQ = sV + kTile;        // 2 stages
   uint8_t* sDO = sQ + 2 * kTile;   // 2 stages
   uint8_t* sP = sDO + 2 * kTile;   // 2 panels
   uint8_t* sDS = sP + 2 * kPanel;  // 2 panels
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sDS + 2 * kPanel);
-  uint64_t* kv_full = bars;        // [2]
-  uint64_t* kv_empty = bars + 2;   // [2]
+  uint8_t* sDQ = sDS + 2 * kPanel; // dQ staging, one 4 KB slot per drain warp
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDQ + kWarpsSm * kDQStage);
+  uint64_t* kv_full = bars;        // [1] (index 1 unused)
+  uint64_t* kv_empty = bars + 2;   // [1]
   uint64_t* qd_full = bars + 4;    // [2]
   uint64_t* qd_empty = bars + 6;   // [2]
   uint64_t* s_full = bars + 8;
@@ -548,8 +548,8 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       int k0, i2, i1, i0;
       int64_t bh;
       item_coords(w, k0, i2, i1, i0, bh);
-      const int kb = it & 1;
-      if (!(pok = mbar_wait_warp(&kv_empty[kb], ((it >> 1) & 1) ^ 1, p.status, kTimeoutProducer, abort_flag))) break;
+      const int kb = 0;  // one K / V buffer: the next item's load waits for this item's last MMA
+      if (!(pok = mbar_wait_warp(&kv_empty[kb], (it & 1) ^ 1, p.status, kTimeoutProducer, abort_flag))) break;
       if (lane == 0) {
         int c[5];
         coords_for(p.kv_pos, k0, i2, i1, i0, c);
@@ -588,9 +588,9 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       int it = 0;
       bool ok = true;
       for (int64_t w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
-        const int kb = it & 1;
-        const uint32_t aK = smem_u32(sK + kb * kTile), aV = smem_u32(sV + kb * kTile);
-        if (!(ok = mbar_wait(&kv_full[kb], (it >> 1) & 1, p.status, kTimeoutMma, abort_flag))) break;
+        const int kb = 0;
+        const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
+        if (!(ok = mbar_wait(&kv_full[kb], it & 1, p.status, kTimeoutMma, abort_flag))) break;
         // S^T / dP^T of block g+1 are issued as soon as the softmax warps have read block
         // g's (s_free), so they run on the tensor core while block g's P / dS are formed
         auto issue_s = [&](int64_t g) -> bool {
@@ -656,8 +656,9 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       item_coords(w, k0, i2, i1, i0, bh);
       const int key = k0 + r;
       const bool key_ok = key < p.Nk;
-      float* dq_b = p.dq + static_cast<int64_t>(i0) * p.dq_s0 + static_cast<int64_t>(i1) * p.dq_s1 +
-                    static_cast<int64_t>(i2) * p.dq_s2;
+      // dQ of a block: TMEM -> this warp's 4 KB shared-memory slot (its 32 query rows x 32
+      // columns, 128B-swizzled) -> one TMA tensor reduce-add into the fp32 accumulator
+      uint8_t* const stg = sDQ + (warp - 4) * kDQStage;
       auto drain_dq = [&](int64_t g, int jj) -> bool {
         if (!mbar_wait_warp(dq_full, g & 1, p.status, kTimeoutEpilogue, abort_flag)) return false;
         tc_fence_after();
@@ -666,14 +667,25 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(dq_free);
-        const int qrow = jj * kM + r;
-        if (qrow < p.Nq) {
-          float* dst = dq_b + static_cast<int64_t>(qrow) * p.dq_row + half * 32;
+        if (lane == 0) {
+          mbar_arrive(dq_free);
+          bulk_wait_read0();  // the slot's previous reduce has read it
+        }
+        __syncwarp();
 #pragma unroll
-          for (int i = 0; i < 32; i += 2)
-            if (half * 32 + i < p.d_valid)
-              red_add_v2(dst + i, __uint_as_float(v[i]) * p.scale, __uint_as_float(v[i + 1]) * p.scale);
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<float4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(v[4 * c]) * p.scale, __uint_as_float(v[4 * c + 1]) * p.scale,
+                          __uint_as_float(v[4 * c + 2]) * p.scale, __uint_as_float(v[4 * c + 3]) * p.scale);
+        fence_proxy_async_smem();
+        __syncwarp();
+        const int row0 = jj * kM + q4 * 32;
+        if (lane == 0 && row0 < p.Nq && half * 32 < p.d_valid) {
+          int c5[5];
+          coords_for(p.dq_pos, row0, i2, i1, i0, c5);
+          c5[0] = half * 32;
+          tma_reduce_add_5d(&tmDQ, stg, c5);
+          bulk_commit();
         }
         return true;
       };
@@ -775,6 +787,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
     }
   }
 
+  if (warp >= 4 && lane == 0) bulk_wait0();  // this warp's dQ reduces have completed
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -793,7 +806,9 @@ struct Map5 {
 
 // Layout (s0, s1, s2, row, d1, d2) of a [.., rows, d] view -> 5-D map with the non-contiguous
 // dimensions sorted by stride (the box is 64 x 1 x .. x 128 rows x ..).
-Map5 make_map(const torch::Tensor& t, const std::vector<int64_t>& l, int64_t n_rows, int64_t n_i0, int d_valid) {
+Map5 make_map(const torch::Tensor& t, const std::vector<int64_t>& l, int64_t n_rows, int64_t n_i0, int d_valid,
+              int elem_bytes = 2, int box_cols = fa::kD, int box_rows = fa::kM,
+              CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   struct Dim {
     int64_t extent, stride;
     int role;  // 0 row, 1 i2, 2 i1, 3 i0
@@ -809,15 +824,15 @@ Map5 make_map(const torch::Tensor& t, const std::vector<int64_t>& l, int64_t n_r
   int64_t ext[5], strides[4];
   int box[5];
   ext[0] = d_valid;
-  box[0] = fa::kD;
+  box[0] = box_cols;
   Map5 m{};
   for (int i = 0; i < 4; ++i) {
     ext[i + 1] = std::max<int64_t>(dims[i].extent, 1);
-    strides[i] = dims[i].stride * 2;
-    box[i + 1] = dims[i].role == 0 ? fa::kM : 1;
+    strides[i] = dims[i].stride * elem_bytes;
+    box[i + 1] = dims[i].role == 0 ? box_rows : 1;
     m.pos[dims[i].role] = i + 1;
   }
-  m.map = make_tmap_nd_bf16(t.data_ptr(), 5, ext, strides, box);
+  m.map = make_tmap_nd_bf16(t.data_ptr(), 5, ext, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, dtype);
   return m;
 }
 
@@ -889,7 +904,8 @@ void attn_bwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
   for (const torch::Tensor* t : std::initializer_list<const torch::Tensor*>{&q, &k, &v, &dout, &dk, &dv})
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16, "attn_bwd_tc: bf16 CUDA tensors");
   TORCH_CHECK(dq.is_cuda() && dq.scalar_type() == at::kFloat, "attn_bwd_tc: dq must be a zeroed fp32 accumulator");
-  for (int i = 0; i < 4; ++i) TORCH_CHECK(ldq[i] % 2 == 0, "attn_bwd_tc: dq rows must be 8-byte aligned");
+  for (int i = 0; i < 4; ++i)
+    TORCH_CHECK(ldq[i] % 4 == 0, "attn_bwd_tc: dq accumulator strides must be multiples of 4 (16-byte TMA reduce)");
   TORCH_CHECK(lse.scalar_type() == at::kFloat && dvec.scalar_type() == at::kFloat, "attn_bwd_tc: fp32 lse / dvec");
   TORCH_CHECK(d_valid > 0 && d_valid <= 64 && d_valid % 8 == 0, "attn_bwd_tc: head dim multiple of 8, <= 64");
   TORCH_CHECK(lq[4] == lkv[4] && lq[5] == lkv[5] && lq[4] == ldo[4] && lq[5] == ldo[5] && lq[4] == ldkv[4] &&
@@ -903,6 +919,8 @@ void attn_bwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
   Map5 mdo = make_map(dout, ldo, Nq, n_i0, static_cast<int>(d_valid));
   Map5 mk = make_map(k, lkv, Nk, n_i0, static_cast<int>(d_valid));
   Map5 mv = make_map(v, lkv, Nk, n_i0, static_cast<int>(d_valid));
+  // fp32 dQ accumulator: 32-column x 32-row boxes (one drain warp's slot), 128B-swizzled
+  Map5 mdq = make_map(dq, ldq, Nq, n_i0, static_cast<int>(d_valid), 4, 32, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
   TORCH_CHECK(std::equal(mq.pos, mq.pos + 4, mdo.pos), "attn_bwd_tc: Q and dO layouts must sort alike");
   AttnBwdTcParams p{};
   p.Nq = static_cast<int>(Nq);
@@ -912,6 +930,7 @@ void attn_bwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   std::copy(mq.pos, mq.pos + 4, p.q_pos);
   std::copy(mk.pos, mk.pos + 4, p.kv_pos);
+  std::copy(mdq.pos, mdq.pos + 4, p.dq_pos);
   p.d1 = static_cast<int>(lq[4]);
   p.d2 = static_cast<int>(lq[5]);
   p.lse = lse.data_ptr<float>();
@@ -940,7 +959,7 @@ void attn_bwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
   if (n_sm[dev] == 0) C10_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev));
   // persistent: one CTA per SM, each looping over (head, key tile) work items
   attn_bwd_tc_kernel<<<static_cast<unsigned>(std::min<int64_t>(p.n_items, n_sm[dev])), fb::kThreads, fb::kSmemBytes,
-                       at::cuda::getCurrentCUDAStream()>>>(mq.map, mk.map, mv.map, mdo.map, p);
+                       at::cuda::getCurrentCUDAStream()>>>(mq.map, mk.map, mv.map, mdo.map, mdq.map, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

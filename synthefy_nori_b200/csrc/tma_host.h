@@ -50,10 +50,12 @@ inline CUtensorMap make_tmap_2d_bf16(void* base, int64_t cols, int64_t rows, int
 
 namespace nori {
 
-// Up-to-5-D bf16 tensor map: dims[0] is the contiguous dimension; strides_bytes[i] is
-// the byte stride of dims[i + 1]; box[i] elements per dimension; 128B swizzle.
+// Up-to-5-D tensor map (bf16 unless `dtype` says otherwise): dims[0] is the contiguous
+// dimension; strides_bytes[i] is the byte stride of dims[i + 1]; box[i] elements per
+// dimension; 128B swizzle.
 inline CUtensorMap make_tmap_nd_bf16(void* base, int rank, const int64_t* dims, const int64_t* strides_bytes,
-                                     const int* box, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+                                     const int* box, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B,
+                                     CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
   TORCH_CHECK(rank >= 1 && rank <= 5, "TMA rank 1..5");
   CUtensorMap m;
@@ -68,7 +70,7 @@ inline CUtensorMap make_tmap_nd_bf16(void* base, int rank, const int64_t* dims, 
     TORCH_CHECK(strides_bytes[i] % 16 == 0, "TMA strides must be multiples of 16 bytes");
     s[i] = static_cast<cuuint64_t>(strides_bytes[i]);
   }
-  CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, base, d, s, b, e,
+  CUresult r = encode_tiled_fn()(&m, dtype, rank, base, d, s, b, e,
                                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (rank ", rank, ") failed with code ", static_cast<int>(r));
