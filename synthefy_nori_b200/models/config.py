@@ -107,6 +107,9 @@ def set_regression_head(cfg: dict, quantiles=None, loss: str = "pinball") -> dic
         qs = list(quantiles if quantiles is not None else QUANTILES_999)
         dec["num_reg_quantiles"] = len(qs)
         dec["regression_quantiles"] = [float(q) for q in qs]
+    elif loss in ("mse", "smooth_l1", "huber"):  # one point prediction per row
+        dec["num_reg_quantiles"] = 1
+        dec.pop("regression_quantiles", None)
     return cfg
 
 

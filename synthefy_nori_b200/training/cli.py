@@ -84,6 +84,10 @@ def _model_config(args) -> dict:
         set_dims(cfg, embed_dim=args.embed_dim, hid_dim=args.hid_dim, nhead=args.nhead, nlayers=args.nlayers)
         apply_v2_lite(cfg)
         finalize_arch_config(cfg)
+    if getattr(args, "loss", "pinball") in ("mse", "smooth_l1", "huber"):
+        from synthefy_nori_b200.models.config import set_regression_head
+
+        set_regression_head(cfg, loss=args.loss)  # point losses train a one-output head
     return cfg
 
 

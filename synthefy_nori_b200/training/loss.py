@@ -105,6 +105,9 @@ def regression_objective(kind: str, pred, target, *, quantiles=None, borders=Non
         if mse_weight > 0:
             per = per + mse_weight * ((bar_expected_value(pred, borders) - t) ** 2).mean(1) / var
         return per.mean()
+    if pred.dim() == 3 and pred.shape[-1] != 1:
+        raise ValueError(f"{kind} needs a single-output regression head (set_regression_head(cfg, loss={kind!r})); "
+                         f"got {pred.shape[-1]} outputs")
     p = pred.float().squeeze(-1) if pred.dim() == 3 else pred.float()
     if kind == "mse":
         e = (p - t) ** 2

@@ -48,13 +48,13 @@ def _run(rank, world, port, q):
 
 
 @pytest.mark.timeout(300)
-def test_sharded_context_matches_single_gpu_cache():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_context_matches_single_gpu_cache(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29700 + (os.getpid() % 500)
+    port = 29100 + (os.getpid() % 500) + 11 * world
     procs = [ctx.Process(target=_run, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()

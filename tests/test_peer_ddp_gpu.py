@@ -44,13 +44,13 @@ def _run(rank, world, port, q):
 
 
 @pytest.mark.timeout(300)
-def test_peer_step_matches_nccl_step():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_step_matches_nccl_step(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + (os.getpid() % 500)
+    port = 29600 + (os.getpid() % 500) + 11 * world
     procs = [ctx.Process(target=_run, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
@@ -59,6 +59,7 @@ def test_peer_step_matches_nccl_step():
         p.join(timeout=60)
         assert p.exitcode == 0
     # ranks agree, and the peer path matches the NCCL path
-    torch.testing.assert_close(res[0][1], res[1][1], atol=0, rtol=0)
-    torch.testing.assert_close(res[0][2], res[1][2], atol=0, rtol=0)
+    for r in res[1:]:  # every rank holds identical weights
+        torch.testing.assert_close(res[0][1], r[1], atol=0, rtol=0)
+        torch.testing.assert_close(res[0][2], r[2], atol=0, rtol=0)
     torch.testing.assert_close(res[0][2], res[0][1], atol=1e-5, rtol=1e-4)

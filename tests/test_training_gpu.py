@@ -8,13 +8,16 @@ pytestmark = pytest.mark.gpu
 
 
 def _setup(**cfg):
-    from synthefy_nori_b200.models.config import preset_config
+    from synthefy_nori_b200.models.config import preset_config, set_regression_head
     from synthefy_nori_b200.training.prior import PriorConfig, scm_prior_batch
     from synthefy_nori_b200.training.trainer import NoriTrainer, TrainConfig
     from synthefy_nori_b200.utils.loading import build_model
 
     torch.manual_seed(0)
-    m = build_model(preset_config("nori-tiny")).cuda()
+    mc = preset_config("nori-tiny")
+    if cfg.get("loss") in ("mse", "smooth_l1", "huber"):
+        set_regression_head(mc, loss=cfg["loss"])
+    m = build_model(mc).cuda()
     tr = NoriTrainer(m, TrainConfig(**cfg), torch.device("cuda"))
     b = scm_prior_batch(PriorConfig(max_features=10, pad_features=10), 4, 128, 96, seed=5, device=torch.device("cuda"))
     return tr, b
