@@ -211,8 +211,9 @@ def run_e2e(args, trainer, shapes, device, world, rank):
     pc = prior_cfg(args)
     B = args.tables_per_gpu
     host = []
+    # the same step shapes as the device-timed steps (shapes[warmup:warmup+steps]), plus one warm-up
     for i in range(args.steps + 1):
-        rows, ep = shapes[i]
+        rows, ep = shapes[args.warmup + i]
         b = scm_prior_batch(pc, B, rows, ep, seed=args.seed * 7 + i + 100 * rank, device=device)
         host.append((b.x.cpu().pin_memory(), b.y.cpu().pin_memory(), ep))
     torch.cuda.synchronize(device)
@@ -560,6 +561,7 @@ def main():
             },
             "clocks": clk,
             "gpu_launches": launches,
+            "peak_mem_gib": round(torch.cuda.max_memory_allocated(device) / 2 ** 30, 1),
             "last_loss": last_loss,
             "wall_s": round(time.time() - t0, 1),
         }

@@ -238,10 +238,14 @@ __device__ __forceinline__ void fwd_store(FwdState& st, __nv_bfloat16* ob, int64
   }
 }
 
+// KV_BUF = 2: K / V tiles double-buffered across the key loop; KV_BUF = 1: the whole key
+// sequence is one tile (short sequences such as the within-row feature attention), so a
+// CTA needs 24 KB instead of 40 KB of shared memory and more CTAs share an SM.
+template <int KV_BUF>
 __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwdParams p) {
   __shared__ __align__(128) uint8_t sq[kBlkQ * 128];
-  __shared__ __align__(128) uint8_t sk[2][kBlkK * 128];
-  __shared__ __align__(128) uint8_t sv[2][kBlkK * 128];
+  __shared__ __align__(128) uint8_t sk[KV_BUF][kBlkK * 128];
+  __shared__ __align__(128) uint8_t sv[KV_BUF][kBlkK * 128];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t bh = blockIdx.x / p.n_tiles_q;
   const int q0 = static_cast<int>(blockIdx.x % p.n_tiles_q) * kBlkQ;
@@ -254,20 +258,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwdParams p)
   load_tile(sv[0], vb, p.lv.row, 0, p.Nk, p.q_d_valid, tid, kAttnThreads);
   cp_async_commit();
 
-  const int n_tiles = (p.Nk + kBlkK - 1) / kBlkK;
   FwdState st;
-  for (int t = 0; t < n_tiles; ++t) {
-    const int buf = t & 1;
-    if (t + 1 < n_tiles) {
-      load_tile(sk[buf ^ 1], kb, p.lk.row, (t + 1) * kBlkK, p.Nk, p.q_d_valid, tid, kAttnThreads);
-      load_tile(sv[buf ^ 1], vb, p.lv.row, (t + 1) * kBlkK, p.Nk, p.q_d_valid, tid, kAttnThreads);
+  if constexpr (KV_BUF == 1) {
+    cp_async_wait<0>();
+    __syncthreads();
+    fwd_init(st, sq, warp, lane);
+    fwd_tile(st, sk[0], sv[0], 0, p.Nk, p.scale_log2, lane);
+  } else {
+    const int n_tiles = (p.Nk + kBlkK - 1) / kBlkK;
+    for (int t = 0; t < n_tiles; ++t) {
+      const int buf = t & 1;
+      if (t + 1 < n_tiles) {
+        load_tile(sk[buf ^ 1], kb, p.lk.row, (t + 1) * kBlkK, p.Nk, p.q_d_valid, tid, kAttnThreads);
+        load_tile(sv[buf ^ 1], vb, p.lv.row, (t + 1) * kBlkK, p.Nk, p.q_d_valid, tid, kAttnThreads);
+      }
+      cp_async_commit();
+      cp_async_wait<1>();
+      __syncthreads();
+      if (t == 0) fwd_init(st, sq, warp, lane);
+      fwd_tile(st, sk[buf], sv[buf], t * kBlkK, p.Nk, p.scale_log2, lane);
+      __syncthreads();
     }
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    if (t == 0) fwd_init(st, sq, warp, lane);
-    fwd_tile(st, sk[buf], sv[buf], t * kBlkK, p.Nk, p.scale_log2, lane);
-    __syncthreads();
   }
   fwd_store(st, p.o + p.lo.offset(bh, 0), p.lo.row, p.lse, bh, q0, p.Nq, p.d_valid, warp, lane);
 }
@@ -652,7 +663,10 @@ void attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
   TORCH_CHECK(BH * p.n_tiles_q < 2147483647LL, "attention grid too large");
   dim3 grid(static_cast<unsigned>(BH * p.n_tiles_q));
   TORCH_CHECK(BH <= 2147483647LL, "attn_fwd: BH too large");
-  attn_fwd_kernel<<<grid, kAttnThreads, 0, at::cuda::getCurrentCUDAStream()>>>(p);
+  if (Nk <= kBlkK)
+    attn_fwd_kernel<1><<<grid, kAttnThreads, 0, at::cuda::getCurrentCUDAStream()>>>(p);
+  else
+    attn_fwd_kernel<2><<<grid, kAttnThreads, 0, at::cuda::getCurrentCUDAStream()>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
