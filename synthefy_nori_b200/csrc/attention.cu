@@ -421,6 +421,7 @@ struct AttnBwdParams {
   const float* lse;
   const float* dvec;
   float* dq;  // fp32 accumulator addressed through ldq
+  __nv_bfloat16* dq16;  // or, with a single key tile, dQ written once in bf16 through ldq
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
   Layout3 lq, lk, lv, ldo, ldk, ldv, ldq;
@@ -572,6 +573,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(AttnBwdParams p)
         }
       }
       const int r0 = q0 + warp * 16 + (lane >> 2);
+      if (p.dq16 != nullptr) {  // single key tile: this CTA owns these dQ rows outright
+        __nv_bfloat16* dqh = p.dq16 + p.ldq.offset(bh, 0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int c = i * 8 + (lane & 3) * 2;
+          if (c >= p.d_valid) continue;
+          if (r0 < p.Nq)
+            *reinterpret_cast<uint32_t*>(dqh + static_cast<int64_t>(r0) * p.ldq.row + c) =
+                pack_bf16x2(dqa[i][0] * p.scale, dqa[i][1] * p.scale);
+          if (r0 + 8 < p.Nq)
+            *reinterpret_cast<uint32_t*>(dqh + static_cast<int64_t>(r0 + 8) * p.ldq.row + c) =
+                pack_bf16x2(dqa[i][2] * p.scale, dqa[i][3] * p.scale);
+        }
+        __syncthreads();
+        continue;
+      }
       float* dqb = p.dq + p.ldq.offset(bh, 0);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -717,9 +734,18 @@ void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
               const torch::Tensor& dout, const torch::Tensor& lse, torch::Tensor& dq, torch::Tensor& dk,
               torch::Tensor& dv, std::vector<int64_t> lq, std::vector<int64_t> lk, std::vector<int64_t> lv,
               std::vector<int64_t> lo, std::vector<int64_t> ldo, std::vector<int64_t> ldk, std::vector<int64_t> ldv,
-              std::vector<int64_t> ldq, int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid, double scale) {
+              std::vector<int64_t> ldq, int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid, double scale,
+              const c10::optional<torch::Tensor>& dq16) {
   for (auto* t : std::initializer_list<const torch::Tensor*>{&q, &k, &v, &o, &dout, &dk, &dv}) check_bf16(*t, "attn_bwd");
-  TORCH_CHECK(dq.is_cuda() && dq.scalar_type() == at::kFloat, "attn_bwd: dq must be a zeroed fp32 accumulator");
+  const bool direct = dq16.has_value() && dq16->defined();
+  if (direct) {
+    check_bf16(*dq16, "attn_bwd dq16");
+    TORCH_CHECK(Nk <= kBlkK, "attn_bwd: a bf16 dQ output needs the keys in one tile (Nk <= 64)");
+    TORCH_CHECK(ldq[3] % 2 == 0 && ldq[0] % 2 == 0 && ldq[1] % 2 == 0 && ldq[2] % 2 == 0,
+                "attn_bwd: bf16 dQ rows must be 4-byte aligned");
+  } else {
+    TORCH_CHECK(dq.is_cuda() && dq.scalar_type() == at::kFloat, "attn_bwd: dq must be a zeroed fp32 accumulator");
+  }
   TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() >= BH * Nq, "attn_bwd: fp32 lse");
   TORCH_CHECK(d_valid > 0 && d_valid <= kD && d_valid % 8 == 0, "attn_bwd: head dim must be a multiple of 8, <= 64");
   const at::cuda::CUDAGuard guard(q.device());
@@ -741,7 +767,8 @@ void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
   p.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
   p.lse = lse.data_ptr<float>();
   p.dvec = dvec.data_ptr<float>();
-  p.dq = dq.data_ptr<float>();
+  p.dq = direct ? nullptr : dq.data_ptr<float>();
+  p.dq16 = direct ? reinterpret_cast<__nv_bfloat16*>(dq16->data_ptr()) : nullptr;
   p.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
   p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
   p.lq = to_layout(lq);

@@ -24,7 +24,8 @@ void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
               const torch::Tensor& dout, const torch::Tensor& lse, torch::Tensor& dq, torch::Tensor& dk,
               torch::Tensor& dv, std::vector<int64_t> lq, std::vector<int64_t> lk, std::vector<int64_t> lv,
               std::vector<int64_t> lo, std::vector<int64_t> ldo, std::vector<int64_t> ldk, std::vector<int64_t> ldv,
-              std::vector<int64_t> ldq, int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid, double scale);
+              std::vector<int64_t> ldq, int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid, double scale,
+              const c10::optional<torch::Tensor>& dq16);
 void attn_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
                  const c10::optional<torch::Tensor>& lse, std::vector<int64_t> lq, std::vector<int64_t> lk,
                  std::vector<int64_t> lv, std::vector<int64_t> lo, int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid,

@@ -600,7 +600,12 @@ torch::Tensor qass_fwd(const torch::Tensor& q, const torch::Tensor& s, const c10
   const int64_t groups = (p.R * p.H + qass::kVec - 1) / qass::kVec;
   const int blocks = static_cast<int>(std::min<int64_t>((groups + qass::kWarps - 1) / qass::kWarps, sm_count(q.get_device()) * 8));
   const int dynf = qass::kWarps * 2 * 16 * 128 + static_cast<int>(H) * 64 * static_cast<int>(sizeof(float));
-  C10_CUDA_CHECK(cudaFuncSetAttribute(qass::qass_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dynf));
+  static int fwd_smem_set[64] = {0};  // once per device (and whenever a larger size is needed)
+  const int dev = q.get_device();
+  if (fwd_smem_set[dev] < dynf) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(qass::qass_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dynf));
+    fwd_smem_set[dev] = dynf;
+  }
   qass::qass_fwd_kernel<<<blocks, qass::kThreads, dynf, at::cuda::getCurrentCUDAStream()>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
@@ -664,7 +669,12 @@ torch::Tensor qass_bwd(const torch::Tensor& q, const torch::Tensor& dout, const 
   const int dyn = 4 * qass::kStageVec * 128 + qass::kWarps * 2 * 16 * 128 +
                   qass::kWarps * 2 * 16 * qass::kDoutLd * static_cast<int>(sizeof(float)) +
                   2 * static_cast<int>(H) * 64 * static_cast<int>(sizeof(float));
-  C10_CUDA_CHECK(cudaFuncSetAttribute(qass::qass_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
+  static int bwd_smem_set[64] = {0};
+  const int dev = q.get_device();
+  if (bwd_smem_set[dev] < dyn) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(qass::qass_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
+    bwd_smem_set[dev] = dyn;
+  }
   qass::qass_bwd_kernel<<<blocks, qass::kThreads, dyn, at::cuda::getCurrentCUDAStream()>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dq;

@@ -129,14 +129,18 @@ def attention_bwd_tc(q, k, v, o, do, lse, dq_f32, dk, dv, *, lq, lkv, lo, ldo, l
 
 
 def attention_bwd(q, k, v, o, do, lse, dq_f32, dk, dv, *, lq, lk, lv, lo, ldo, ldk, ldv, BH, Nq, Nk, d, scale,
-                  ldq=None):
+                  ldq=None, dq_bf16=None):
     """Flash attention backward. ``dq_f32`` is a zeroed fp32 accumulator addressed through
-    ``ldq`` (default: head-major ``[BH, Nq, 64]``); dK / dV are written through their layouts."""
+    ``ldq`` (default: head-major ``[BH, Nq, 64]``); dK / dV are written through their layouts.
+    With ``dq_bf16`` (only for ``Nk <= 64``: one key tile, so each dQ row has one writer)
+    dQ is written there in bf16 through ``ldq`` and ``dq_f32`` is not used."""
     if ldq is None:
         ldq = (Nq * 64, 0, 0, 64, 1, 1)
+    if dq_bf16 is not None:
+        dq_f32 = dq_bf16.new_empty(0, dtype=torch.float32)
     _lib().attn_bwd(q, k, v, o, do, lse, dq_f32, dk, dv, _layout(lq), _layout(lk), _layout(lv), _layout(lo),
                     _layout(ldo), _layout(ldk), _layout(ldv), _layout(ldq), int(BH), int(Nq), int(Nk), int(d),
-                    float(scale))
+                    float(scale), dq_bf16)
 
 
 def rms_scale(x: torch.Tensor, eps: float) -> torch.Tensor:

@@ -373,12 +373,17 @@ class FeatSublayer(torch.autograd.Function):
         n_rows = x.shape[0] // g.T
         BH = n_rows * g.H
         dy = torch.empty(x.shape[0], 3 * E, device=dev, dtype=BF16)
-        dq32 = torch.zeros(x.shape[0], E, device=dev, dtype=torch.float32)
         l3, l1 = _feat_layout(g, 3 * E), _feat_layout(g, E)
-        ops.attention_bwd(y[:, :E], y[:, E : 2 * E], y[:, 2 * E :], o, do, lse, dq32, dy[:, E : 2 * E], dy[:, 2 * E :],
-                          lq=l3, lk=l3, lv=l3, lo=l1, ldo=l1, ldk=l3, ldv=l3, ldq=l1, BH=BH, Nq=g.T, Nk=g.T, d=D,
-                          scale=scale)
-        dy[:, :E] = dq32
+        if g.T <= 64:  # one key tile: dQ goes straight into dy in bf16 (no fp32 accumulator)
+            ops.attention_bwd(y[:, :E], y[:, E : 2 * E], y[:, 2 * E :], o, do, lse, None, dy[:, E : 2 * E],
+                              dy[:, 2 * E :], lq=l3, lk=l3, lv=l3, lo=l1, ldo=l1, ldk=l3, ldv=l3, ldq=l3, BH=BH,
+                              Nq=g.T, Nk=g.T, d=D, scale=scale, dq_bf16=dy[:, :E])
+        else:
+            dq32 = torch.zeros(x.shape[0], E, device=dev, dtype=torch.float32)
+            ops.attention_bwd(y[:, :E], y[:, E : 2 * E], y[:, 2 * E :], o, do, lse, dq32, dy[:, E : 2 * E],
+                              dy[:, 2 * E :], lq=l3, lk=l3, lv=l3, lo=l1, ldo=l1, ldk=l3, ldv=l3, ldq=l1, BH=BH,
+                              Nq=g.T, Nk=g.T, d=D, scale=scale)
+            dy[:, :E] = dq32
         xn = ops.rms_apply(x, rs)
         dw_qkv = torch.zeros(3 * E, E, device=dev, dtype=torch.float32)
         ops.gemm_wgrad(dy, xn, dw_qkv)
@@ -435,10 +440,24 @@ def check_supported(model) -> None:
             )
 
 
+def _layer_alpha(layer) -> float:
+    """The DeepNorm residual scale as a host float, read from its (device) buffer only when
+    the buffer changes (reading it is a device synchronisation)."""
+    buf = getattr(layer, "deepnorm_alpha", None)
+    if buf is None:
+        return 1.0
+    key = (buf.data_ptr(), buf._version)
+    hit = getattr(layer, "_nori_alpha", None)
+    if hit is None or hit[0] != key:
+        hit = (key, float(buf))
+        layer._nori_alpha = hit
+    return hit[1]
+
+
 def run_layer(layer, x: torch.Tensor, g: Geometry, stash: dict | None = None) -> torch.Tensor:
     w = layer_weights(layer)
     wb = _cached_bf16(layer, w)
-    alpha = layer.alpha
+    alpha = _layer_alpha(layer)
     eps = layer.layer_norm_eps
     qp = list(w["qp"])
     x = SeqSublayer.apply(x, w["w_ctx"], w["w_q"], w["wo_self"], w["wo_cross"], g, alpha, eps, w["qmode"], wb, stash,
@@ -472,7 +491,11 @@ def run_stack_tokens(model, x: torch.Tensor, g: Geometry, checkpoint_layers: boo
     stash_on = checkpoint_layers and torch.is_grad_enabled() and stash_attention and _stash_fits(model, g, x.device)
     for layer in model.transformer_encoder.layers:
         if checkpoint_layers and torch.is_grad_enabled():
-            x = checkpoint(run_layer, layer, x, g, {} if stash_on else None, use_reentrant=False)
+            # no randomness inside a layer (no dropout), so the RNG state is not saved and
+            # restored around the recomputation (doing so reads the CUDA generator state on
+            # the host, a device synchronisation per layer)
+            x = checkpoint(run_layer, layer, x, g, {} if stash_on else None, use_reentrant=False,
+                           preserve_rng_state=False)
         else:
             x = run_layer(layer, x, g)
     return x
@@ -536,7 +559,7 @@ class NativeKV:
 def _seq_ctx_forward(layer, w, x, g: Geometry):
     """Sequence sublayer over context-only rows; returns (x_out, cross K/V [R_ctx, 2E])."""
     E, D = g.E, g.D
-    eps, alpha = layer.layer_norm_eps, layer.alpha
+    eps, alpha = layer.layer_norm_eps, _layer_alpha(layer)
     rs = ops.rms_scale(x, eps)
     wb = w["wb"]
     y = ops.gemm(x, wb["w_ctx"], row_scale=rs)
@@ -558,7 +581,7 @@ def _attn(q, k, v, o, lq, lkv, lo, BH, Nq, Nk, D, lse=None):
 def _mlp_forward(layer, w, x):
     rs = ops.rms_scale(x, layer.layer_norm_eps)
     h = ops.gemm_swiglu(x, w["wb"]["w_gu"], row_scale=rs)
-    return ops.gemm_residual(h, w["wb"]["w_down"], x, layer.alpha)
+    return ops.gemm_residual(h, w["wb"]["w_down"], x, _layer_alpha(layer))
 
 
 @torch.no_grad()
@@ -571,7 +594,7 @@ def _feat_forward(layer, w, x, g: Geometry):
     l3, l1 = _feat_layout(g, 3 * E), _feat_layout(g, E)
     ops.attention_fwd(y[:, :E], y[:, E : 2 * E], y[:, 2 * E :], o, lq=l3, lk=l3, lv=l3, lo=l1, BH=n_rows * g.H, Nq=g.T,
                       Nk=g.T, d=D, scale=1.0 / math.sqrt(D))
-    return ops.gemm_residual(o, w["wb"]["w_fo_t"], x, layer.alpha)
+    return ops.gemm_residual(o, w["wb"]["w_fo_t"], x, _layer_alpha(layer))
 
 
 @torch.no_grad()
@@ -635,4 +658,4 @@ def _seq_query_forward(layer, w, x, kv: NativeKV, g: Geometry, lse=None, partial
         _attn(q, kv.kv[:, :E], kv.kv[:, E:], o, lq, l2, lq, BTH, g.nq, g.ep, D, lse=lse)
     if partial_out is not None:  # context-sharded inference merges partial outputs first
         return partial_out(o)
-    return ops.gemm_residual(o, w["wb"]["wo_cross_t"], x, layer.alpha)
+    return ops.gemm_residual(o, w["wb"]["wo_cross_t"], x, _layer_alpha(layer))

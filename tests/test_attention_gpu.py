@@ -51,6 +51,14 @@ def test_headmajor_fwd_bwd(BH, Nq, Nk):
     torch.testing.assert_close(dk.float(), kf.grad, atol=5e-2, rtol=5e-2)
     torch.testing.assert_close(dv.float(), vf.grad, atol=5e-2, rtol=5e-2)
     assert dq[..., D:].abs().max().item() == 0
+    if Nk <= 64:  # one key tile: dQ written straight to bf16, equal to the fp32 accumulator's
+        dq16 = torch.zeros(BH, Nq, D, device="cuda", dtype=torch.bfloat16)
+        dk2, dv2 = torch.empty_like(dk), torch.empty_like(dv)
+        ops.attention_bwd(q, k, v, o, do, lse, None, dk2, dv2, lq=hm(Nq), lk=hm(Nk), lv=hm(Nk), lo=tm(Nq),
+                          ldo=tm(Nq), ldk=tm(Nk), ldv=tm(Nk), ldq=tm(Nq), BH=BH, Nq=Nq, Nk=Nk, d=D, scale=scale,
+                          dq_bf16=dq16)
+        torch.testing.assert_close(dq16.float(), dq[..., :D].to(torch.bfloat16).float(), atol=1e-2, rtol=1e-2)
+        assert torch.equal(dk2, dk) and torch.equal(dv2, dv)
 
 
 def test_token_major_sequence_and_feature_layouts():
