@@ -82,6 +82,7 @@ void adamw_ema(torch::Tensor& p, const torch::Tensor& g, torch::Tensor& m, torch
                const c10::optional<torch::Tensor>& norm_sq, double lr, double beta1, double beta2, double eps,
                double wd, int64_t step, double ema_decay, double max_norm, double grad_scale);
 std::vector<torch::Tensor> quantize_int8(const torch::Tensor& x);
+void dequantize_int8(const torch::Tensor& q, const torch::Tensor& scale, torch::Tensor& out);
 }  // namespace nori
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -117,4 +118,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_sumsq", &nori::grad_sumsq);
   m.def("adamw_ema", &nori::adamw_ema);
   m.def("quantize_int8", &nori::quantize_int8);
+  m.def("dequantize_int8", &nori::dequantize_int8);
 }

@@ -484,6 +484,44 @@ std::vector<torch::Tensor> quantize_int8(const torch::Tensor& x) {
   return {q, sc};
 }
 
+// q int8 [R, D] with scale fp32 [R] -> bf16 [R, D] = bf16(float(q) * scale), the same
+// rounding as dequantising in PyTorch (int8 -> fp32 multiply -> bf16). D % 8 == 0: each
+// thread converts 8 values (one 8-byte load, one 16-byte store), all under one scale.
+__global__ void dequant_int8_kernel(const int8_t* __restrict__ q, const float* __restrict__ scale, int64_t n8, int D,
+                                    __nv_bfloat16* __restrict__ out) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = i * 8;
+    const float s = __ldg(scale + e / D);
+    const int2 raw = __ldg(reinterpret_cast<const int2*>(q + e));
+    const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
+    uint4 packed;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&packed);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      o2[j] = __floats2bfloat162_rn(static_cast<float>(b[2 * j]) * s, static_cast<float>(b[2 * j + 1]) * s);
+    *reinterpret_cast<uint4*>(out + e) = packed;
+  }
+}
+
+void dequantize_int8(const torch::Tensor& q, const torch::Tensor& scale, torch::Tensor& out) {
+  TORCH_CHECK(q.is_cuda() && q.is_contiguous() && q.scalar_type() == at::kChar, "dequantize_int8: contiguous int8 q");
+  TORCH_CHECK(scale.is_contiguous() && scale.scalar_type() == at::kFloat, "dequantize_int8: contiguous fp32 scale");
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16 && out.numel() == q.numel(),
+              "dequantize_int8: contiguous bf16 output of q's size");
+  const int64_t n = q.numel();
+  TORCH_CHECK(n == 0 || n % scale.numel() == 0, "dequantize_int8: q rows must match the scales");
+  if (n == 0) return;
+  const int D = static_cast<int>(n / scale.numel());
+  TORCH_CHECK(D % 8 == 0, "dequantize_int8: row length must be a multiple of 8");
+  const at::cuda::CUDAGuard guard(q.device());
+  const int64_t n8 = n / 8;
+  const int blocks = static_cast<int>(std::min<int64_t>((n8 + 255) / 256, 148 * 32));
+  dequant_int8_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      q.data_ptr<int8_t>(), scale.data_ptr<float>(), n8, D, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // ------------------------------------------------------------------ quantile collapse
 // Per row: sort the K predicted quantiles ascending (monotone quantile function), the
 // trapezoid mean of the piecewise-linear quantile function with flat tails

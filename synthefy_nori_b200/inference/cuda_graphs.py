@@ -31,6 +31,10 @@ class GraphedQueryRunner:
         self.graph = torch.cuda.CUDAGraph()
         with torch.no_grad(), torch.cuda.graph(self.graph):
             self.out = self.model.apply_context_cache(self.x, self.context, return_hidden=return_hidden)
+        from synthefy_nori_b200.ops import fused_layer
+
+        # the graph writes the int8 cache's bf16 expansion into the shared scratch by address
+        self._scratch = dict(fused_layer._DEQUANT_SCRATCH)
 
     @torch.no_grad()
     def __call__(self, xq: torch.Tensor) -> torch.Tensor:

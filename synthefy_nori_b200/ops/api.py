@@ -28,6 +28,7 @@ __all__ = [
     "grad_sumsq",
     "adamw_ema_step",
     "quantize_int8",
+    "dequantize_int8",
     "status_word",
     "check_status",
     "interleave_swiglu_weights",
@@ -186,6 +187,14 @@ def quantize_int8(x: torch.Tensor):
     """Per-row (last dim) absmax int8: returns (q int8, scale fp32 with last dim 1)."""
     q, s = _lib().quantize_int8(x.contiguous())
     return q, s
+
+
+def dequantize_int8(q: torch.Tensor, scale: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``bf16(float(q) * scale)`` for int8 ``q [..., D]`` with one fp32 scale per row of D."""
+    if out is None:
+        out = torch.empty(q.shape, device=q.device, dtype=torch.bfloat16)
+    _lib().dequantize_int8(q.contiguous(), scale.contiguous(), out)
+    return out
 
 
 def qass_fwd(q, s, w1=None, b1=None, w2=None, b2=None, *, H: int, D: int):

@@ -548,11 +548,40 @@ class NativeKV:
         q, s = ops.quantize_int8(kv.reshape(kv.shape[0], 2, g.H, g.D))
         return cls(q.reshape(kv.shape[0], 2 * g.E), g, s.reshape(kv.shape[0], 2 * g.H))
 
-    def dequantize(self) -> torch.Tensor:
+    def dequantize(self, out: torch.Tensor | None = None) -> torch.Tensor:
         if self.scale is None:
             return self.kv
         g = self.g
+        if self.kv.is_cuda and ops.native_available():
+            return ops.dequantize_int8(self.kv, self.scale, out)
         return (self.kv.view(-1, 2, g.H, g.D).float() * self.scale.view(-1, 2, g.H, 1)).to(BF16).view(-1, 2 * g.E)
+
+
+# bf16 scratch for the dequantised K/V of one layer, shared by all layers of a query pass
+_DEQUANT_SCRATCH: dict = {}
+DEQUANT_SCRATCH_MAX_FRACTION = 0.25
+
+
+def _dequant_scratch(kv: NativeKV) -> torch.Tensor | None:
+    """A bf16 buffer of ``kv``'s shape, or None when it would take more than a quarter of
+    the free device memory (the int8 kernel then reads the cache directly)."""
+    dev = kv.kv.device
+    n = kv.kv.numel()
+    buf = _DEQUANT_SCRATCH.get(dev)
+    if buf is not None and buf.numel() >= n:
+        return buf[:n].view(kv.kv.shape)
+    free, _ = torch.cuda.mem_get_info(dev)
+    if 2 * n > DEQUANT_SCRATCH_MAX_FRACTION * free:
+        return None
+    _DEQUANT_SCRATCH.pop(dev, None)
+    buf = torch.empty(n, device=dev, dtype=BF16)
+    _DEQUANT_SCRATCH[dev] = buf
+    return buf.view(kv.kv.shape)
+
+
+def release_dequant_scratch() -> None:
+    """Free the shared dequantisation buffers (they are reused across query passes)."""
+    _DEQUANT_SCRATCH.clear()
 
 
 @torch.no_grad()
@@ -647,7 +676,15 @@ def _seq_query_forward(layer, w, x, kv: NativeKV, g: Geometry, lse=None, partial
     o = torch.empty(x.shape[0], E, device=x.device, dtype=BF16)
     lq = _seq_layout(g.nq, g, E)
     BTH = g.B * g.T * g.H
-    if kv.quantized:
+    scratch = _dequant_scratch(kv) if kv.quantized else None
+    if scratch is not None:
+        # one GPU: expand the int8 cache to bf16 (a memory-bound pass, ~1/50 of the attention
+        # time) so the query attention runs on the tcgen05 kernel; same values as the
+        # reference's dequantise-then-attend
+        kvb = kv.dequantize(scratch)
+        l2 = _seq_layout(g.ep, g, 2 * E)
+        _attn(q, kvb[:, :E], kvb[:, E:], o, lq, l2, lq, BTH, g.nq, g.ep, D, lse=lse)
+    elif kv.quantized:
         l2 = _seq_layout(g.ep, g, 2 * E)
         ls = (g.ep * g.T * 2 * g.H, 2 * g.H, 1, g.T * 2 * g.H, g.T, g.H)
         # one-shard case of the multi-shard kernel (register-pipelined int8 tile loads)

@@ -69,3 +69,11 @@ def test_quantize_int8_bit_exact():
     qref = torch.clamp(torch.round(x / scale), -127, 127).to(torch.int8)
     assert torch.equal(q, qref)
     torch.testing.assert_close(s, scale, atol=0, rtol=0)
+
+
+def test_dequantize_int8_bit_exact():
+    x = torch.randn(300, 2, 8, 56, device="cuda")
+    q, s = ops.quantize_int8(x)
+    out = ops.dequantize_int8(q.view(300, -1), s.view(300, -1))
+    ref = (q.float() * s).to(torch.bfloat16).view(300, -1)
+    assert out.dtype == torch.bfloat16 and torch.equal(out, ref)

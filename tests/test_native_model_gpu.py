@@ -107,6 +107,26 @@ def test_native_context_cache_matches_full_forward(dtype):
     assert (out - ref).abs().max().item() < 0.08 * ref.abs().max().item() + 0.05
 
 
+def test_int8_cache_dequantised_path_matches_int8_kernel(monkeypatch):
+    """One GPU expands the int8 cache to bf16 and attends on the tcgen05 kernel; with no
+    room for the expansion the int8 kernel reads the cache directly. Both agree."""
+    from synthefy_nori_b200.ops import fused_layer
+
+    m = _model("nori-tiny").eval()
+    x, y, ep = _data(B=1, S=400, F=7, ep=300)
+    with torch.no_grad():
+        cache = m.build_context_cache(x[:, :ep], y[:, :ep], cache_dtype="int8")
+        fused_layer.release_dequant_scratch()
+        a = m.apply_context_cache(x[:, ep:], cache).float()
+        assert fused_layer._DEQUANT_SCRATCH  # the expansion path ran
+        fused_layer.release_dequant_scratch()
+        monkeypatch.setattr(fused_layer, "DEQUANT_SCRATCH_MAX_FRACTION", 0.0)
+        b = m.apply_context_cache(x[:, ep:], cache).float()
+        assert not fused_layer._DEQUANT_SCRATCH
+    assert _cos(a, b) > 0.9999
+    assert (a - b).abs().max().item() < 0.02 * b.abs().max().item() + 0.01
+
+
 def test_int8_attention_kernel_matches_dequantized():
     import math
 
