@@ -62,17 +62,23 @@ struct AttnTcParams {
   int* status;
 };
 
-// 2^x for x <= 0 on the FMA pipe: x = n + f (n = floor x, f in [0, 1)),
-// 2^f ~ c0 + c1 f + c2 f^2 + c3 f^3 (least-squares fit at Chebyshev nodes on [0, 1),
-// max relative error 7.8e-5, well under bf16's 2^-8), 2^n added to the exponent bits.
+// 2^x for x <= 0 without the XU pipe (the MUFU, float->int conversions and rounding all
+// issue there, and the softmax already keeps it busy with ex2 and bf16 packing):
+//   t = x + 1.5 * 2^23 rounds x to the nearest integer n, which then sits in the low
+//   mantissa bits of t (FADD); f = x - n in [-0.5, 0.5];
+//   2^f ~ c0 + c1 f + c2 f^2 + c3 f^3 (minimax in relative error on [-0.5, 0.5], fitted for
+//   this kernel: max relative error 7.5e-5, well under bf16's 2^-9);
+//   2^n enters as (bits of t) << 23 added to the exponent field (integer ALU).
+// x is clamped at -125 so the scaled result stays a normal float.
 __device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float n = floorf(x);
-  const float f = x - n;
-  float pl = fmaf(f, 0.07790716737508774f, 0.22623319923877716f);
-  pl = fmaf(pl, f, 0.6957771182060242f);
-  pl = fmaf(pl, f, 0.999927818775177f);
-  return __int_as_float(__float_as_int(pl) + (static_cast<int>(n) << 23));
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x = fmaxf(x, -125.0f);
+  const float t = x + kRound;
+  const float f = x - (t - kRound);
+  float pl = fmaf(f, 0.0551716648042202f, 0.2426111251115799f);
+  pl = fmaf(pl, f, 0.6932609677314758f);
+  pl = fmaf(pl, f, 0.9999280571937561f);
+  return __uint_as_float(__float_as_uint(pl) + (__float_as_uint(t) << 23));
 }
 
 // 2^x on the MUFU (one instruction; flushes subnormal results to zero, which the bf16 P
@@ -81,6 +87,56 @@ __device__ __forceinline__ float exp2_mufu(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed fp32 pairs (sm_100 f32x2 instructions: two lanes of FMA-pipe work per issue).
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// exp2_poly on a packed pair: the rounding, reduction and polynomial run as f32x2.
+__device__ __forceinline__ void exp2_poly2(uint64_t x2, float& e0, float& e1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  float x0, x1;
+  f2unpack(x2, x0, x1);
+  x2 = f2pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t r2 = f2pack(kRound, kRound);
+  const uint64_t t2 = f2add(x2, r2);
+  const uint64_t f2 = f2sub(x2, f2sub(t2, r2));
+  uint64_t pl = f2fma(f2, f2pack(0.0551716648042202f, 0.0551716648042202f),
+                      f2pack(0.2426111251115799f, 0.2426111251115799f));
+  pl = f2fma(pl, f2, f2pack(0.6932609677314758f, 0.6932609677314758f));
+  pl = f2fma(pl, f2, f2pack(0.9999280571937561f, 0.9999280571937561f));
+  float p0, p1, t0, t1;
+  f2unpack(pl, p0, p1);
+  f2unpack(t2, t0, t1);
+  e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
 __device__ __forceinline__ void coords_for(const int (&pos)[4], int row, int i2, int i1, int i0, int (&c)[5]) {
@@ -309,12 +365,17 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         float mx = -INFINITY;
         if (full_tile) {
           // tree reduction: eight independent chains instead of one 64-long dependency chain
+          // (three-input max: two values per instruction)
           float m8[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) m8[i] = fmaxf(__uint_as_float(v0[i]), __uint_as_float(v1[i]));
+          for (int i = 0; i < 8; ++i) m8[i] = fmax3(__uint_as_float(v0[i]), __uint_as_float(v1[i]), __uint_as_float(v0[i + 8]));
 #pragma unroll
-          for (int i = 8; i < 32; ++i) m8[i & 7] = fmaxf(m8[i & 7], fmaxf(__uint_as_float(v0[i]), __uint_as_float(v1[i])));
-          mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+          for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], __uint_as_float(v1[i + 8]), __uint_as_float(v0[i + 16]));
+#pragma unroll
+          for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], __uint_as_float(v1[i + 16]), __uint_as_float(v0[i + 24]));
+#pragma unroll
+          for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], __uint_as_float(v1[i + 24]));
+          mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
@@ -340,14 +401,31 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
           const uint32_t(&v)[32] = c == 0 ? v0 : v1;
           uint32_t pk[16];
           if (full_tile) {
+            const uint64_t sc2 = f2pack(p.scale_log2, p.scale_log2), nm2 = f2pack(nm, nm);
+            uint64_t rsa = 0, rsb = 0;  // packed partial row sums (+0.0f, +0.0f)
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              // even columns on the MUFU, odd columns on the FMA pipe (polynomial 2^x)
-              const float e0 = exp2_mufu(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, nm));
-              const float e1 = exp2_poly(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, nm));
-              pk[i] = pack_bf16x2(e0, e1);
-              rs[i & 3] += e0 + e1;
+            for (int i = 0; i < 8; ++i) {
+              // columns 4i, 4i+1 on the MUFU, 4i+2, 4i+3 on the FMA pipe (polynomial 2^x);
+              // scaling, reduction and row sums as packed f32x2
+              const uint64_t xa = f2fma(f2pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])), sc2, nm2);
+              const uint64_t xb =
+                  f2fma(f2pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])), sc2, nm2);
+              float xa0, xa1, e2, e3;
+              f2unpack(xa, xa0, xa1);
+              const float e0 = exp2_mufu(xa0), e1 = exp2_mufu(xa1);
+              exp2_poly2(xb, e2, e3);
+              pk[2 * i] = pack_bf16x2(e0, e1);
+              pk[2 * i + 1] = pack_bf16x2(e2, e3);
+              rsa = f2add(rsa, f2pack(e0, e1));
+              rsb = f2add(rsb, f2pack(e2, e3));
             }
+            float r0, r1, r2, r3;
+            f2unpack(rsa, r0, r1);
+            f2unpack(rsb, r2, r3);
+            rs[0] += r0;
+            rs[1] += r1;
+            rs[2] += r2;
+            rs[3] += r3;
           } else {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {

@@ -3,7 +3,7 @@
     python -m synthefy_nori_b200.ops.microbench gemm  --m 131072 --n 1344 --k 448 [--epi store|swiglu|residual|dgrad|wgrad]
     python -m synthefy_nori_b200.ops.microbench attn  --bh 128 --n 2048 --d 56 [--kernel tc|mma|bwd|bwdtc]
     python -m synthefy_nori_b200.ops.microbench attn  --bh 19200 --n 51 --d 56 --kernel feat|featbwd   (rows x 8 heads)
-    python -m synthefy_nori_b200.ops.microbench qass  --rows 262144 --h 8 --d 56
+    python -m synthefy_nori_b200.ops.microbench qass  --rows 262144 --h 8 --d 56 [--kernel fwd|bwd]
     python -m synthefy_nori_b200.ops.microbench step  --model nori-100m --tables 16 --rows 1200 --ctx 800 --features 100
 
 ``step`` prints the per-kernel device time of one training step (torch.profiler CUDA
@@ -141,6 +141,12 @@ def bench_qass(a):
     s = torch.rand(H, D, device="cuda") + 1
     w1, b1 = torch.randn(64, D, device="cuda") * 0.1, torch.zeros(64, device="cuda")
     w2, b2 = torch.randn(D, 64, device="cuda") * 0.1, torch.zeros(D, device="cuda")
+    if a.kernel == "bwd":
+        dout = torch.randn(R, H * D, device="cuda")
+        gs = torch.zeros(H, D, device="cuda")
+        g = [torch.zeros_like(t) for t in (w1, b1, w2, b2)]
+        fn = lambda: ops.qass_bwd(q, dout, s, gs, w1, b1, w2, b2, *g, H=H, D=D)  # noqa: E731
+        return fn, 2.0 * 5 * R * H * D * 64
     fn = lambda: ops.qass_fwd(q, s, w1, b1, w2, b2, H=H, D=D)  # noqa: E731
     return fn, 2.0 * 2 * R * H * D * 64
 
@@ -175,7 +181,7 @@ def step_breakdown(a) -> None:
     for ev in prof.key_averages():
         t = getattr(ev, "self_device_time_total", 0)
         if t > 0:
-            rows.append((t / 1000.0, ev.count, ev.key[:90]))
+            rows.append((t / 1000.0, ev.count, ev.key[: a.width]))
     rows.sort(reverse=True)
     tot = sum(r[0] for r in rows)
     print(f"unprofiled step {step_ms:.1f} ms; kernels in the profiled step {tot:.1f} ms, "
@@ -202,6 +208,7 @@ def main():
     qa.add_argument("--rows", type=int, default=262144)
     qa.add_argument("--h", type=int, default=8)
     qa.add_argument("--d", type=int, default=56)
+    qa.add_argument("--kernel", default="fwd", help="fwd | bwd")
     for p in (g, t, qa):
         p.add_argument("--launches", type=int, default=0)
     st = sub.add_parser("step")
@@ -211,6 +218,7 @@ def main():
     st.add_argument("--ctx", type=int, default=800)
     st.add_argument("--features", type=int, default=100)
     st.add_argument("--top", type=int, default=30)
+    st.add_argument("--width", type=int, default=90, help="characters of each kernel name")
     a = ap.parse_args()
     if a.what == "step":
         step_breakdown(a)
