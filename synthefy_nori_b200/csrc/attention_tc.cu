@@ -10,15 +10,17 @@
 //               3-stage rings (K(j) is released when S_j completes, V(j) when O_j
 //               completes; 5-D tensor maps read the strided token-major layouts
 //               directly; head-dim padding and tails are zero-filled by TMA);
-//   warp 1      TMEM owner + MMA issuer: S_j = Q K_j^T (M=128, N=128, K=64) into one
-//               of two TMEM score buffers, then O_j = P_j V_j (M=128, N=64, K=128,
-//               V read MN-major) into one of two TMEM output buffers;
-//   warps 4..7  softmax: one thread per query row (its TMEM lane); reads S_j, keeps
-//               the running max / sum, writes P_j (bf16) to shared memory in the
-//               128B-swizzled K-major layout the MMA reads, and accumulates
-//               O += alpha * O_j in registers.
-// Score tile j+1 is computed by the tensor core while the softmax of tile j runs.
-//
+//   warp 1      TMEM owner + MMA issuer: S_j = Q K_j^T (M=128, N=128, K=64) into the
+//               score buffer of group j % 2, then O_g += P_j V_j (M=128, N=64, K=128,
+//               V read MN-major) into that group's TMEM accumulator; order S_0, S_1,
+//               PV_0, S_2, PV_1, S_3, ... so a score tile is always in flight;
+//   warps 4..7 / 8..11  two softmax groups, one per key-tile parity, each with its own
+//               running max / sum: thread = query row (its TMEM lane), all 128 columns;
+//               P_j (bf16) goes to shared memory in the 128B-swizzled K-major layout the
+//               MMA reads.  The max is lazy (O_g is rescaled in TMEM only when a row's
+//               max grows by more than 2^8), and the groups merge their (max, sum,
+//               O_g) once per item.  The two groups work on different tiles at the same
+//               time, so one group's waits overlap the other's arithmetic.
 // Every mbarrier wait is bounded (see sm100.cuh); on timeout the CTA records an error
 // in the status word and returns after freeing its TMEM.
 #include <ATen/cuda/CUDAContext.h>
@@ -147,6 +149,68 @@ __device__ __forceinline__ void coords_for(const int (&pos)[4], int row, int i2,
   c[pos[3]] = i0;
 }
 
+// Row maximum of 64 score columns (two 32-column TMEM loads), `valid` of them real.
+__device__ __forceinline__ float rowmax64(const uint32_t (&va)[32], const uint32_t (&vb)[32], int valid) {
+  if (valid >= 64) {
+    float m8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      m8[i] = fmax3(__uint_as_float(va[i]), __uint_as_float(va[i + 8]), __uint_as_float(va[i + 16]));
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      m8[i] = fmax3(m8[i], __uint_as_float(va[i + 24]), __uint_as_float(vb[i]));
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      m8[i] = fmax3(m8[i], __uint_as_float(vb[i + 8]), __uint_as_float(vb[i + 16]));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], __uint_as_float(vb[i + 24]));
+    return fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+  }
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if (i < valid) m = fmaxf(m, __uint_as_float(va[i]));
+    if (32 + i < valid) m = fmaxf(m, __uint_as_float(vb[i]));
+  }
+  return m;
+}
+
+// P = 2^(s scale_log2 + nm) for 32 score columns -> 16 packed bf16 pairs; returns the row
+// sum of the (fp32) values. Columns at or past `valid` give 0.
+__device__ __forceinline__ float softmax_chunk32(const uint32_t (&v)[32], int valid, float scale_log2, float nm,
+                                                 uint32_t (&pk)[16]) {
+  if (valid >= 32) {
+    const uint64_t sc2 = f2pack(scale_log2, scale_log2), nm2 = f2pack(nm, nm);
+    uint64_t rsa = 0, rsb = 0;  // packed partial row sums (+0.0f, +0.0f)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      // columns 4i, 4i+1 on the MUFU, 4i+2, 4i+3 on the FMA pipe (polynomial 2^x)
+      const uint64_t xa = f2fma(f2pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])), sc2, nm2);
+      const uint64_t xb = f2fma(f2pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])), sc2, nm2);
+      float xa0, xa1, e2, e3;
+      f2unpack(xa, xa0, xa1);
+      const float e0 = exp2_mufu(xa0), e1 = exp2_mufu(xa1);
+      exp2_poly2(xb, e2, e3);
+      pk[2 * i] = pack_bf16x2(e0, e1);
+      pk[2 * i + 1] = pack_bf16x2(e2, e3);
+      rsa = f2add(rsa, f2pack(e0, e1));
+      rsb = f2add(rsb, f2pack(e2, e3));
+    }
+    float r0, r1;
+    f2unpack(f2add(rsa, rsb), r0, r1);
+    return r0 + r1;
+  }
+  float rs = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float e0 = 2 * i < valid ? exp2_mufu(fmaf(__uint_as_float(v[2 * i]), scale_log2, nm)) : 0.f;
+    const float e1 = 2 * i + 1 < valid ? exp2_mufu(fmaf(__uint_as_float(v[2 * i + 1]), scale_log2, nm)) : 0.f;
+    pk[i] = pack_bf16x2(e0, e1);
+    rs += e0 + e1;
+  }
+  return rs;
+}
+
 __global__ void __launch_bounds__(fa::kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, AttnTcParams p) {
@@ -156,24 +220,23 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   uint8_t* sQ = smem;                             // 2 buffers (consecutive work items)
   uint8_t* sK = sQ + 2 * kTileBytes;              // kStages
   uint8_t* sV = sK + kStages * kTileBytes;        // kStages
-  uint8_t* sP = sV + kStages * kTileBytes;        // 2 buffers of 32 KB
+  uint8_t* sP = sV + kStages * kTileBytes;        // one 32 KB P tile per softmax group
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
   uint64_t* q_full = bars;        // [2]
   uint64_t* q_empty = bars + 2;   // [2]
-  uint64_t* s_full = bars + 4;    // [2]
-  uint64_t* p_full = bars + 6;    // [2]
-  uint64_t* o_full = bars + 8;    // [2]
-  uint64_t* o_free = bars + 10;   // [2]
-  uint64_t* xbar = bars + 12;     // [2] row-max exchange between the two column halves
-  uint64_t* sbar = bars + 14;     // [2] row-sum exchange at the end of a work item
-  uint64_t* k_full = bars + 16;   // [kStages]
-  uint64_t* k_empty = bars + 19;  // [kStages]
-  uint64_t* v_full = bars + 22;   // [kStages]
-  uint64_t* v_empty = bars + 25;  // [kStages]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
+  uint64_t* s_full = bars + 4;    // [group]
+  uint64_t* p_full = bars + 6;    // [group]
+  uint64_t* o_full = bars + 8;    // [group]
+  uint64_t* o_free = bars + 10;   // [group] both accumulators read by the item's epilogue
+  uint64_t* sbar = bars + 12;     // [item parity] (max, sum) exchange at the end of an item
+  uint64_t* k_full = bars + 14;   // [kStages]
+  uint64_t* k_empty = bars + 17;  // [kStages]
+  uint64_t* v_full = bars + 20;   // [kStages]
+  uint64_t* v_empty = bars + 23;  // [kStages]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 26);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  __shared__ float red_max[2][2][kM];  // [tile parity][column half][row]
-  __shared__ float red_sum[2][2][kM];  // [item parity][column half][row]
+  __shared__ float red_m[2][2][kM];  // [item parity][group][row]
+  __shared__ float red_l[2][2][kM];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_tiles = (p.Nk + kN - 1) / kN;
@@ -192,10 +255,9 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], kSoftmaxWarps);
+      mbar_init(&p_full[i], kSoftmaxWarps / 2);
       mbar_init(&o_full[i], 1);
       mbar_init(&o_free[i], kSoftmaxWarps);
-      mbar_init(&xbar[i], kSoftmaxWarps);
       mbar_init(&sbar[i], kSoftmaxWarps);
     }
     *abort_flag = 0;
@@ -206,8 +268,8 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem;            // S buffers at columns 0, 128
-  const uint32_t tO = tmem + 2 * kN;   // O buffers at columns 256, 320
+  const uint32_t tS = tmem;            // S buffers (one per group) at columns 0, 128
+  const uint32_t tO = tmem + 2 * kN;   // O accumulators (one per group) at columns 256, 320
 
   // work item w -> (head bh, query tile); items are visited with stride gridDim.x
   auto item_coords = [&](int64_t w, int& q0, int& i2, int& i1, int& i0, int64_t& bh) {
@@ -264,225 +326,222 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
     if (elect_one()) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(kM, kN, false, false);
       constexpr uint32_t idesc_o = umma_idesc_bf16(kM, kD, false, true);
-      int64_t gk = 0, gv = 0, gt = 0;  // K / V ring positions, global tile index (S / P / O buffers)
+      int64_t gk = 0, gv = 0;     // K / V ring positions
+      int64_t cnt[2] = {0, 0};    // tiles per group so far (s_full / p_full / o_full completions)
       int it = 0;
       bool ok = true;
       for (int64_t w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
         const int qb = it & 1;
         if (!(ok = mbar_wait(&q_full[qb], (it >> 1) & 1, p.status, kTimeoutMma, abort_flag))) break;
         const uint32_t aQ = smem_u32(sQ + qb * kTileBytes);
-        const int64_t t0 = gt;  // global index of this item's first tile
-        auto issue_s = [&](int64_t g) -> bool {
-          const int s = static_cast<int>(g & 1), st = static_cast<int>(gk % kStages);
+        // S of the group's next key tile into that group's score buffer
+        auto issue_s = [&](int grp) -> bool {
+          const int st = static_cast<int>(gk % kStages);
           if (!mbar_wait(&k_full[st], (gk / kStages) & 1, p.status, kTimeoutMma, abort_flag)) return false;
           tc_fence_after();
           const uint32_t bK = smem_u32(sK + st * kTileBytes);
 #pragma unroll
           for (int k = 0; k < kD / 16; ++k)
-            umma_bf16_ss(tS + s * kN, umma_desc_kmajor_sw128(aQ + k * 32), umma_desc_kmajor_sw128(bK + k * 32),
+            umma_bf16_ss(tS + grp * kN, umma_desc_kmajor_sw128(aQ + k * 32), umma_desc_kmajor_sw128(bK + k * 32),
                          idesc_s, k > 0 ? 1u : 0u);
-          umma_commit(&s_full[s]);
+          umma_commit(&s_full[grp]);
           umma_commit(&k_empty[st]);
           ++gk;
           return true;
         };
-        ok = issue_s(t0);
-        for (int j = 0; ok && j < n_tiles; ++j, ++gt) {
-          const int s = static_cast<int>(gt & 1);
-          if (j + 1 < n_tiles) {
-            if (!(ok = issue_s(gt + 1))) break;
-          } else {
-            umma_commit(&q_empty[qb]);  // the item's last score MMA read Q
-          }
+        ok = issue_s(0);
+        if (ok && n_tiles > 1) ok = issue_s(1);
+        if (ok && n_tiles <= 2) umma_commit(&q_empty[qb]);  // every score MMA of the item read Q
+        for (int j = 0; ok && j < n_tiles; ++j) {
+          const int grp = j & 1;
+          const bool first = j < 2;  // the group's first tile of this item starts its accumulator
+          if (!(ok = mbar_wait(&p_full[grp], cnt[grp] & 1, p.status, kTimeoutMma, abort_flag))) break;
+          if (first && it > 0 &&
+              !(ok = mbar_wait(&o_free[grp], (it - 1) & 1, p.status, kTimeoutMma, abort_flag)))
+            break;
           const int st = static_cast<int>(gv % kStages);
-          if (!(ok = mbar_wait(&p_full[s], (gt >> 1) & 1, p.status, kTimeoutMma, abort_flag))) break;
-          if (gt >= 2 && !(ok = mbar_wait(&o_free[s], ((gt >> 1) & 1) ^ 1, p.status, kTimeoutMma, abort_flag))) break;
           if (!(ok = mbar_wait(&v_full[st], (gv / kStages) & 1, p.status, kTimeoutMma, abort_flag))) break;
           tc_fence_after();
-          const uint32_t aP = smem_u32(sP + s * kPBytes);
+          const uint32_t aP = smem_u32(sP + grp * kPBytes);
           const uint32_t bV = smem_u32(sV + st * kTileBytes);
 #pragma unroll
           for (int k = 0; k < kN / 16; ++k) {
             const uint64_t da = umma_desc_kmajor_sw128(aP + (k >> 2) * (kM * 128) + (k & 3) * 32);
             const uint64_t db = umma_smem_desc(bV + k * 2048, 8192, 1024, 2);
-            umma_bf16_ss(tO + s * kD, da, db, idesc_o, k > 0 ? 1u : 0u);
+            umma_bf16_ss(tO + grp * kD, da, db, idesc_o, (k > 0 || !first) ? 1u : 0u);
           }
-          umma_commit(&o_full[s]);
+          umma_commit(&o_full[grp]);
           umma_commit(&v_empty[st]);
           ++gv;
+          ++cnt[grp];
+          if (j + 2 < n_tiles) {
+            ok = issue_s(grp);
+            if (ok && j + 2 == n_tiles - 1) umma_commit(&q_empty[qb]);
+          }
         }
       }
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax
-    // Two warps per TMEM lane quarter: `half` selects score columns [64 half, 64 half + 64)
-    // (= P panel `half`) and output columns [32 half, 32 half + 32).
+    // Group g (warps 4..7 -> 0, 8..11 -> 1) takes the key tiles j = g, g + 2, ... of each
+    // item with its own running max / sum and its own TMEM accumulator O_g; thread = query
+    // row (its TMEM lane), all 128 score columns. The max is lazy: O_g and the sum are
+    // rescaled only when a row's max grows by more than 2^8, so P values stay <= 256
+    // (exact enough in bf16) and most tiles skip the rescale. At the end of the item the
+    // two groups exchange (max, sum) and each writes half of the output columns from
+    // both accumulators.
+    constexpr float kRescaleLog2 = 8.0f;
+    const int grp = (warp - 4) >> 2;
     const int q = warp & 3;
-    const int half = (warp - 4) >> 2;
     const int r = q * 32 + lane;  // row in tile == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t tSg = tS + grp * kN + lane_off;
+    const uint32_t tOg = tO + grp * kD + lane_off;
+    uint8_t* const Pg = sP + grp * kPBytes;
     bool ok = true;
-    int64_t gt = 0;  // global tile index (matches the MMA warp's)
+    int64_t cnt = 0;  // this group's tiles so far (barrier completions)
     int it = 0;
     for (int64_t w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
       int q0, i2, i1, i0;
       int64_t bh;
       item_coords(w, q0, i2, i1, i0, bh);
-      float m_cur = -INFINITY, l = 0.f;
-      float o[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) o[i] = 0.f;
-      auto absorb = [&](int64_t g, float a) -> bool {
-        const int s = static_cast<int>(g & 1);
-        if (!mbar_wait_warp(&o_full[s], (g >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) return false;
-        tc_fence_after();
-        uint32_t v[32];
-        tmem_ld32(tO + s * kD + lane_off + half * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = o[i] * a + __uint_as_float(v[i]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&o_free[s]);
-        return true;
-      };
-      float alpha_pending = 1.f;
-      for (int j = 0; ok && j < n_tiles; ++j, ++gt) {
-        const int s = static_cast<int>(gt & 1);
-        const uint32_t ph = static_cast<uint32_t>((gt >> 1) & 1);
-        if (!mbar_wait_warp(&s_full[s], ph, p.status, kTimeoutEpilogue, abort_flag)) {
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = grp; ok && j < n_tiles; j += 2, ++cnt) {
+        if (!mbar_wait_warp(&s_full[grp], cnt & 1, p.status, kTimeoutEpilogue, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int valid = min(kN, p.Nk - j * kN) - half * 64;  // valid columns of this half
-        const uint32_t ts = tS + s * kN + lane_off + half * 64;
-        uint32_t v0[32], v1[32];
-        tmem_ld32(ts, v0);
-        tmem_ld32(ts + 32, v1);
-        tmem_wait_ld();
-        const bool full_tile = valid >= 64;
-        float mx = -INFINITY;
-        if (full_tile) {
-          // tree reduction: eight independent chains instead of one 64-long dependency chain
-          // (three-input max: two values per instruction)
-          float m8[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) m8[i] = fmax3(__uint_as_float(v0[i]), __uint_as_float(v1[i]), __uint_as_float(v0[i + 8]));
-#pragma unroll
-          for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], __uint_as_float(v1[i + 8]), __uint_as_float(v0[i + 16]));
-#pragma unroll
-          for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], __uint_as_float(v1[i + 16]), __uint_as_float(v0[i + 24]));
-#pragma unroll
-          for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], __uint_as_float(v1[i + 24]));
-          mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
-        } else {
+        const int valid = min(kN, p.Nk - j * kN);
+        float mx;
+        {  // pass 1: row max
+          uint32_t va[32], vb[32];
+          tmem_ld32(tSg, va);
+          tmem_ld32(tSg + 32, vb);
+          tmem_wait_ld();
+          mx = rowmax64(va, vb, valid);
+          if (valid > 64) {
+            tmem_ld32(tSg + 64, va);
+            tmem_ld32(tSg + 96, vb);
+            tmem_wait_ld();
+            mx = fmaxf(mx, rowmax64(va, vb, valid - 64));
+          }
+        }
+        const float m_cand = mx * p.scale_log2;
+        // the group's previous P . V (same P buffer, same accumulator) must be complete
+        // before P is overwritten or O rescaled
+        if (cnt > 0 && !mbar_wait_warp(&o_full[grp], (cnt - 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) {
+          ok = false;
+          break;
+        }
+        float a = 1.f;
+        bool need = false;
+        if (j == grp) {
+          m_used = m_cand;  // first tile: the accumulator starts fresh
+        } else if (m_cand > m_used + kRescaleLog2) {
+          a = exp2f(m_used - m_cand);
+          m_used = m_cand;
+          need = true;
+        }
+        if (__any_sync(0xffffffffu, need)) {  // warp-collective TMEM read-modify-write of O_g
+          tc_fence_after();
+          uint32_t o0[32], o1[32];
+          tmem_ld32(tOg, o0);
+          tmem_ld32(tOg + 32, o1);
+          tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            if (i < valid) mx = fmaxf(mx, __uint_as_float(v0[i]));
-            if (32 + i < valid) mx = fmaxf(mx, __uint_as_float(v1[i]));
+            o0[i] = __float_as_uint(__uint_as_float(o0[i]) * a);
+            o1[i] = __float_as_uint(__uint_as_float(o1[i]) * a);
           }
+          tmem_st32(tOg, o0);
+          tmem_st32(tOg + 32, o1);
+          tmem_wait_st();
         }
-        red_max[s][half][r] = mx;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&xbar[s]);
-        if (!mbar_wait_warp(&xbar[s], ph, p.status, kTimeoutEpilogue, abort_flag)) {
-          ok = false;
-          break;
-        }
-        mx = fmaxf(mx, red_max[s][half ^ 1][r]);
-        const float m_new = fmaxf(m_cur, mx * p.scale_log2);
-        const float a = exp2f(m_cur - m_new);  // m_cur = -inf on the first tile -> 0
-        const float nm = -m_new;
-        float rs[4] = {0.f, 0.f, 0.f, 0.f};  // four partial row sums (short dependency chains)
-        uint8_t* panel = sP + s * kPBytes + half * (kM * 128);
+        l *= a;
+        // pass 2: P (bf16) into the two 64-key panels, 128B-swizzled K-major
+        const float nm = -m_used;
+        float rsum = 0.f;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint32_t(&v)[32] = c == 0 ? v0 : v1;
+        for (int c2 = 0; c2 < 2; ++c2) {
+          if (c2 * 64 >= valid) {  // an all-padding panel: zeros
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc)
+              *reinterpret_cast<uint4*>(Pg + c2 * (kM * 128) + r * 128 + ((cc ^ (r & 7)) << 4)) =
+                  make_uint4(0u, 0u, 0u, 0u);
+            continue;
+          }
+          uint32_t va[32], vb[32];
+          tmem_ld32(tSg + c2 * 64, va);
+          tmem_ld32(tSg + c2 * 64 + 32, vb);
+          tmem_wait_ld();
           uint32_t pk[16];
-          if (full_tile) {
-            const uint64_t sc2 = f2pack(p.scale_log2, p.scale_log2), nm2 = f2pack(nm, nm);
-            uint64_t rsa = 0, rsb = 0;  // packed partial row sums (+0.0f, +0.0f)
+          rsum += softmax_chunk32(va, valid - c2 * 64, p.scale_log2, nm, pk);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              // columns 4i, 4i+1 on the MUFU, 4i+2, 4i+3 on the FMA pipe (polynomial 2^x);
-              // scaling, reduction and row sums as packed f32x2
-              const uint64_t xa = f2fma(f2pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])), sc2, nm2);
-              const uint64_t xb =
-                  f2fma(f2pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])), sc2, nm2);
-              float xa0, xa1, e2, e3;
-              f2unpack(xa, xa0, xa1);
-              const float e0 = exp2_mufu(xa0), e1 = exp2_mufu(xa1);
-              exp2_poly2(xb, e2, e3);
-              pk[2 * i] = pack_bf16x2(e0, e1);
-              pk[2 * i + 1] = pack_bf16x2(e2, e3);
-              rsa = f2add(rsa, f2pack(e0, e1));
-              rsb = f2add(rsb, f2pack(e2, e3));
-            }
-            float r0, r1, r2, r3;
-            f2unpack(rsa, r0, r1);
-            f2unpack(rsb, r2, r3);
-            rs[0] += r0;
-            rs[1] += r1;
-            rs[2] += r2;
-            rs[3] += r3;
-          } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int col = c * 32 + 2 * i;
-              const float e0 = col < valid ? exp2_mufu(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, nm)) : 0.f;
-              const float e1 =
-                  col + 1 < valid ? exp2_poly(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, nm)) : 0.f;
-              pk[i] = pack_bf16x2(e0, e1);
-              rs[i & 3] += e0 + e1;
-            }
-          }
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            const int chunk = c * 4 + cc;
-            *reinterpret_cast<uint4*>(panel + r * 128 + ((chunk ^ (r & 7)) << 4)) =
+          for (int cc = 0; cc < 4; ++cc)
+            *reinterpret_cast<uint4*>(Pg + c2 * (kM * 128) + r * 128 + ((cc ^ (r & 7)) << 4)) =
                 make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
-          }
+          rsum += softmax_chunk32(vb, valid - c2 * 64 - 32, p.scale_log2, nm, pk);
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc)
+            *reinterpret_cast<uint4*>(Pg + c2 * (kM * 128) + r * 128 + (((4 + cc) ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
         }
-        l = l * a + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+        l += rsum;
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[s]);
-        if (j >= 1 && !absorb(gt - 1, alpha_pending)) {
-          ok = false;
-          break;
-        }
-        alpha_pending = a;
-        m_cur = m_new;
+        if (lane == 0) mbar_arrive(&p_full[grp]);
       }
-      if (ok) ok = absorb(gt - 1, alpha_pending);
-      red_sum[it & 1][half][r] = l;
+      // epilogue: this group's last P . V done, exchange (max, sum), combine the accumulators
+      const bool has1 = n_tiles > 1;
+      if (ok && (grp == 0 || has1))
+        ok = mbar_wait_warp(&o_full[grp], (cnt - 1) & 1, p.status, kTimeoutEpilogue, abort_flag);
+      red_m[it & 1][grp][r] = m_used;
+      red_l[it & 1][grp][r] = l;
       __syncwarp();
       if (lane == 0) mbar_arrive(&sbar[it & 1]);
       if (ok) ok = mbar_wait_warp(&sbar[it & 1], (it >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag);
       if (ok) {
-        const float lt = red_sum[it & 1][0][r] + red_sum[it & 1][1][r];
+        tc_fence_after();
+        const float m0 = red_m[it & 1][0][r], l0 = red_l[it & 1][0][r];
+        const float m1 = has1 ? red_m[it & 1][1][r] : -INFINITY, l1 = has1 ? red_l[it & 1][1][r] : 0.f;
+        const float m = fmaxf(m0, m1);
+        const float f0 = exp2f(m0 - m), f1 = has1 ? exp2f(m1 - m) : 0.f;
+        const float lt = l0 * f0 + l1 * f1;
+        uint32_t a0[32], a1[32];
+        tmem_ld32(tO + lane_off + grp * 32, a0);
+        if (has1) tmem_ld32(tO + kD + lane_off + grp * 32, a1);
+        tmem_wait_ld();
         const int row = q0 + r;
         if (row < p.Nq) {
           const float inv = lt > 0.f ? 1.f / lt : 0.f;
+          const float g0 = f0 * inv, g1 = f1 * inv;
+          float o[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            o[i] = __uint_as_float(a0[i]) * g0 + (has1 ? __uint_as_float(a1[i]) * g1 : 0.f);
           __nv_bfloat16* out = p.o + static_cast<int64_t>(i0) * p.o_s0 + static_cast<int64_t>(i1) * p.o_s1 +
-                               static_cast<int64_t>(i2) * p.o_s2 + static_cast<int64_t>(row) * p.o_row + half * 32;
+                               static_cast<int64_t>(i2) * p.o_s2 + static_cast<int64_t>(row) * p.o_row + grp * 32;
 #pragma unroll
           for (int c8 = 0; c8 < 4; ++c8) {
-            if (half * 32 + c8 * 8 < p.d_valid) {
+            if (grp * 32 + c8 * 8 < p.d_valid) {
               *reinterpret_cast<uint4*>(out + c8 * 8) =
-                  make_uint4(pack_bf16x2(o[c8 * 8] * inv, o[c8 * 8 + 1] * inv),
-                             pack_bf16x2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv),
-                             pack_bf16x2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv),
-                             pack_bf16x2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv));
+                  make_uint4(pack_bf16x2(o[c8 * 8], o[c8 * 8 + 1]), pack_bf16x2(o[c8 * 8 + 2], o[c8 * 8 + 3]),
+                             pack_bf16x2(o[c8 * 8 + 4], o[c8 * 8 + 5]), pack_bf16x2(o[c8 * 8 + 6], o[c8 * 8 + 7]));
             }
           }
-          if (p.lse != nullptr && half == 0) {
+          if (p.lse != nullptr && grp == 0) {
             constexpr float kLn2 = 0.6931471805599453f;
-            p.lse[bh * p.Nq + row] = lt > 0.f ? (m_cur + log2f(lt)) * kLn2 : -INFINITY;
+            p.lse[bh * p.Nq + row] = lt > 0.f ? (m + log2f(lt)) * kLn2 : -INFINITY;
           }
         }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&o_free[0]);
+        mbar_arrive(&o_free[1]);
       }
     }
   }
