@@ -42,12 +42,17 @@ constexpr int kD = 64;       // padded head dim
 constexpr int kThreads = 384;  // warps 0 (TMA), 1 (MMA), 4..11 (softmax)
 
 constexpr int kSoftmaxWarps = 8;  // softmax-side barriers take one arrive per warp
+// register split of the forward kernel (launch: 384 threads x 168 = 64512), made inside each
+// role's branch: warps 0..3 (TMA, MMA, two idle) give up to kRegsLow, the eight softmax
+// warps take kRegsSoftmax
+constexpr uint32_t kRegsLow = 48, kRegsSoftmax = 224;
+static_assert(4 * 32 * kRegsLow + 8 * 32 * kRegsSoftmax <= kThreads * 168, "register split over the launch total");
 constexpr int kTileBytes = kM * kD * 2;  // 16 KB (Q, K or V tile)
 constexpr int kPBytes = kM * kN * 2;     // 32 KB (P tile: two 64-key panels)
 constexpr int kStages = 3;  // K and V rings (separate: K(j) frees after S_j, V(j) after O_j)
 // smem: Q[2] | K[3] | V[3] | P[2] | barriers
 constexpr int kSmemBytes = kTileBytes * (2 + 2 * kStages) + kPBytes * 2 + 1024 + 256;
-constexpr uint32_t kTmemCols = 512;  // S[2] (2 x 128) + O[2] (2 x 64) -> 384 used
+constexpr uint32_t kTmemCols = 512;  // S[2] (2 x 128) + O[item parity][group] (4 x 64)
 }  // namespace fa
 
 struct AttnTcParams {
@@ -227,7 +232,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   uint64_t* s_full = bars + 4;    // [group]
   uint64_t* p_full = bars + 6;    // [group]
   uint64_t* o_full = bars + 8;    // [group]
-  uint64_t* o_free = bars + 10;   // [group] both accumulators read by the item's epilogue
+  uint64_t* o_free = bars + 10;   // [item parity] that item's accumulators read by its epilogue
   uint64_t* sbar = bars + 12;     // [item parity] (max, sum) exchange at the end of an item
   uint64_t* k_full = bars + 14;   // [kStages]
   uint64_t* k_empty = bars + 17;  // [kStages]
@@ -269,7 +274,9 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem;            // S buffers (one per group) at columns 0, 128
-  const uint32_t tO = tmem + 2 * kN;   // O accumulators (one per group) at columns 256, 320
+  // O accumulators: two sets (item parity) of one per group, at columns 256 + 128 set + 64 group,
+  // so the next item's P . V products overlap this item's epilogue
+  const uint32_t tO = tmem + 2 * kN;
 
   // work item w -> (head bh, query tile); items are visited with stride gridDim.x
   auto item_coords = [&](int64_t w, int& q0, int& i2, int& i1, int& i0, int64_t& bh) {
@@ -281,6 +288,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   };
 
   if (warp == 0) {
+    setmaxnreg_dec<kRegsLow>();
     if (elect_one()) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -323,6 +331,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
       }
     }
   } else if (warp == 1) {
+    setmaxnreg_dec<kRegsLow>();
     if (elect_one()) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(kM, kN, false, false);
       constexpr uint32_t idesc_o = umma_idesc_bf16(kM, kD, false, true);
@@ -356,8 +365,8 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
           const int grp = j & 1;
           const bool first = j < 2;  // the group's first tile of this item starts its accumulator
           if (!(ok = mbar_wait(&p_full[grp], cnt[grp] & 1, p.status, kTimeoutMma, abort_flag))) break;
-          if (first && it > 0 &&
-              !(ok = mbar_wait(&o_free[grp], (it - 1) & 1, p.status, kTimeoutMma, abort_flag)))
+          if (first && it >= 2 &&
+              !(ok = mbar_wait(&o_free[qb], ((it >> 1) - 1) & 1, p.status, kTimeoutMma, abort_flag)))
             break;
           const int st = static_cast<int>(gv % kStages);
           if (!(ok = mbar_wait(&v_full[st], (gv / kStages) & 1, p.status, kTimeoutMma, abort_flag))) break;
@@ -368,7 +377,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
           for (int k = 0; k < kN / 16; ++k) {
             const uint64_t da = umma_desc_kmajor_sw128(aP + (k >> 2) * (kM * 128) + (k & 3) * 32);
             const uint64_t db = umma_smem_desc(bV + k * 2048, 8192, 1024, 2);
-            umma_bf16_ss(tO + grp * kD, da, db, idesc_o, (k > 0 || !first) ? 1u : 0u);
+            umma_bf16_ss(tO + (qb * 2 + grp) * kD, da, db, idesc_o, (k > 0 || !first) ? 1u : 0u);
           }
           umma_commit(&o_full[grp]);
           umma_commit(&v_empty[st]);
@@ -381,7 +390,10 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         }
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp < 4) {
+    setmaxnreg_dec<kRegsLow>();  // idle warps 2, 3 take part in their warpgroup's split
+  } else {
+    setmaxnreg_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax
     // Group g (warps 4..7 -> 0, 8..11 -> 1) takes the key tiles j = g, g + 2, ... of each
     // item with its own running max / sum and its own TMEM accumulator O_g; thread = query
@@ -396,7 +408,6 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
     const int r = q * 32 + lane;  // row in tile == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t tSg = tS + grp * kN + lane_off;
-    const uint32_t tOg = tO + grp * kD + lane_off;
     uint8_t* const Pg = sP + grp * kPBytes;
     bool ok = true;
     int64_t cnt = 0;  // this group's tiles so far (barrier completions)
@@ -405,6 +416,8 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
       int q0, i2, i1, i0;
       int64_t bh;
       item_coords(w, q0, i2, i1, i0, bh);
+      const uint32_t tOi = tO + (it & 1) * 2 * kD;  // this item's accumulator set
+      const uint32_t tOg = tOi + grp * kD + lane_off;
       float m_used = -INFINITY, l = 0.f;
       for (int j = grp; ok && j < n_tiles; j += 2, ++cnt) {
         if (!mbar_wait_warp(&s_full[grp], cnt & 1, p.status, kTimeoutEpilogue, abort_flag)) {
@@ -413,20 +426,15 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         }
         tc_fence_after();
         const int valid = min(kN, p.Nk - j * kN);
-        float mx;
-        {  // pass 1: row max
-          uint32_t va[32], vb[32];
-          tmem_ld32(tSg, va);
-          tmem_ld32(tSg + 32, vb);
-          tmem_wait_ld();
-          mx = rowmax64(va, vb, valid);
-          if (valid > 64) {
-            tmem_ld32(tSg + 64, va);
-            tmem_ld32(tSg + 96, vb);
-            tmem_wait_ld();
-            mx = fmaxf(mx, rowmax64(va, vb, valid - 64));
-          }
-        }
+        // the whole 128-column score row in registers (one TMEM round trip)
+        uint32_t va[32], vb[32], vc[32], vd[32];
+        tmem_ld32(tSg, va);
+        tmem_ld32(tSg + 32, vb);
+        tmem_ld32(tSg + 64, vc);
+        tmem_ld32(tSg + 96, vd);
+        tmem_wait_ld();
+        float mx = rowmax64(va, vb, valid);
+        if (valid > 64) mx = fmaxf(mx, rowmax64(vc, vd, valid - 64));
         const float m_cand = mx * p.scale_log2;
         // the group's previous P . V (same P buffer, same accumulator) must be complete
         // before P is overwritten or O rescaled
@@ -443,50 +451,48 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
           m_used = m_cand;
           need = true;
         }
-        if (__any_sync(0xffffffffu, need)) {  // warp-collective TMEM read-modify-write of O_g
-          tc_fence_after();
-          uint32_t o0[32], o1[32];
-          tmem_ld32(tOg, o0);
-          tmem_ld32(tOg + 32, o1);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            o0[i] = __float_as_uint(__uint_as_float(o0[i]) * a);
-            o1[i] = __float_as_uint(__uint_as_float(o1[i]) * a);
-          }
-          tmem_st32(tOg, o0);
-          tmem_st32(tOg + 32, o1);
-          tmem_wait_st();
-        }
-        l *= a;
-        // pass 2: P (bf16) into the two 64-key panels, 128B-swizzled K-major
+        // P (bf16) into the two 64-key panels, 128B-swizzled K-major
         const float nm = -m_used;
         float rsum = 0.f;
-#pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          if (c2 * 64 >= valid) {  // an all-padding panel: zeros
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc)
-              *reinterpret_cast<uint4*>(Pg + c2 * (kM * 128) + r * 128 + ((cc ^ (r & 7)) << 4)) =
-                  make_uint4(0u, 0u, 0u, 0u);
-            continue;
-          }
-          uint32_t va[32], vb[32];
-          tmem_ld32(tSg + c2 * 64, va);
-          tmem_ld32(tSg + c2 * 64 + 32, vb);
-          tmem_wait_ld();
+        {
           uint32_t pk[16];
-          rsum += softmax_chunk32(va, valid - c2 * 64, p.scale_log2, nm, pk);
+          rsum += softmax_chunk32(va, valid, p.scale_log2, nm, pk);
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc)
-            *reinterpret_cast<uint4*>(Pg + c2 * (kM * 128) + r * 128 + ((cc ^ (r & 7)) << 4)) =
+            *reinterpret_cast<uint4*>(Pg + r * 128 + ((cc ^ (r & 7)) << 4)) =
                 make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
-          rsum += softmax_chunk32(vb, valid - c2 * 64 - 32, p.scale_log2, nm, pk);
+          rsum += softmax_chunk32(vb, valid - 32, p.scale_log2, nm, pk);
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc)
-            *reinterpret_cast<uint4*>(Pg + c2 * (kM * 128) + r * 128 + (((4 + cc) ^ (r & 7)) << 4)) =
+            *reinterpret_cast<uint4*>(Pg + r * 128 + (((4 + cc) ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+          rsum += softmax_chunk32(vc, valid - 64, p.scale_log2, nm, pk);
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc)
+            *reinterpret_cast<uint4*>(Pg + kM * 128 + r * 128 + ((cc ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+          rsum += softmax_chunk32(vd, valid - 96, p.scale_log2, nm, pk);
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc)
+            *reinterpret_cast<uint4*>(Pg + kM * 128 + r * 128 + (((4 + cc) ^ (r & 7)) << 4)) =
                 make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
         }
+        // O_g rescale after P left the registers (warp-collective TMEM read-modify-write;
+        // lanes that keep their max scale by 1)
+        if (__any_sync(0xffffffffu, need)) {
+          tc_fence_after();
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t o[32];
+            tmem_ld32(tOg + h * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * a);
+            tmem_st32(tOg + h * 32, o);
+          }
+          tmem_wait_st();
+        }
+        l = l * a;
         l += rsum;
         fence_proxy_async_smem();
         tc_fence_before();
@@ -510,8 +516,8 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         const float f0 = exp2f(m0 - m), f1 = has1 ? exp2f(m1 - m) : 0.f;
         const float lt = l0 * f0 + l1 * f1;
         uint32_t a0[32], a1[32];
-        tmem_ld32(tO + lane_off + grp * 32, a0);
-        if (has1) tmem_ld32(tO + kD + lane_off + grp * 32, a1);
+        tmem_ld32(tOi + lane_off + grp * 32, a0);
+        if (has1) tmem_ld32(tOi + kD + lane_off + grp * 32, a1);
         tmem_wait_ld();
         const int row = q0 + r;
         if (row < p.Nq) {
@@ -540,8 +546,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&o_free[0]);
-        mbar_arrive(&o_free[1]);
+        mbar_arrive(&o_free[it & 1]);
       }
     }
   }
