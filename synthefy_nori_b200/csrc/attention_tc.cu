@@ -120,6 +120,11 @@ __device__ __forceinline__ uint64_t f2sub(uint64_t a, uint64_t b) {
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -633,7 +638,8 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // per-stage query vectors: LSE (log2 units) and Dvec of the block's 128 queries
-  __shared__ float s_lse[2][kM], s_dv[2][kM];
+  __shared__ __align__(16) float s_lse[2][kM];
+  __shared__ __align__(16) float s_dv[2][kM];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_qt = (p.Nq + kM - 1) / kM;
@@ -713,7 +719,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         }
         for (int i = lane; i < kM; i += 32) {
           const int qi = j * kM + i;
-          s_lse[s][i] = qi < p.Nq ? lse_g[qi] * kLog2e : INFINITY;
+          s_lse[s][i] = qi < p.Nq ? -lse_g[qi] * kLog2e : -INFINITY;  // negated: added in the exponent
           s_dv[s][i] = qi < p.Nq ? dv_g[qi] : 0.f;
         }
         __syncwarp();
@@ -861,30 +867,71 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         const int qbase = j * kM + half * 64;
         uint8_t* panelP = sP + half * kPanel;
         uint8_t* panelS = sDS + half * kPanel;
+        if (key_ok && qbase + 64 <= p.Nq) {
+          // every column valid: scaling, the polynomial 2^x (half of the columns; the other
+          // half on the MUFU) and dS = P (dP - D) as packed f32x2
+          const uint64_t sc2 = f2pack(p.scale_log2, p.scale_log2);
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          uint32_t pk[4], dk4[4];
+          for (int ch = 0; ch < 8; ++ch) {
+            uint32_t pk[4], dk4[4];
 #pragma unroll
-          for (int i2p = 0; i2p < 4; ++i2p) {
-            float pe[2], de[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int col = ch * 8 + i2p * 2 + e;
-              const int qi = qbase + col;
-              float pv = 0.f, ds = 0.f;
-              if (key_ok && qi < p.Nq) {
-                pv = exp2_mufu(fmaf(__uint_as_float(sv[col]), p.scale_log2, -sl[col]));
-                ds = pv * (__uint_as_float(dp[col]) - sd[col]);
-              }
-              pe[e] = pv;
-              de[e] = ds;
+            for (int h = 0; h < 2; ++h) {
+              const int c0 = ch * 8 + h * 4;
+              const float2 la = *reinterpret_cast<const float2*>(sl + c0);
+              const float2 lb = *reinterpret_cast<const float2*>(sl + c0 + 2);
+              const float2 da = *reinterpret_cast<const float2*>(sd + c0);
+              const float2 db = *reinterpret_cast<const float2*>(sd + c0 + 2);
+              const uint64_t xa = f2fma(f2pack(__uint_as_float(sv[c0]), __uint_as_float(sv[c0 + 1])), sc2,
+                                        f2pack(la.x, la.y));
+              const uint64_t xb = f2fma(f2pack(__uint_as_float(sv[c0 + 2]), __uint_as_float(sv[c0 + 3])), sc2,
+                                        f2pack(lb.x, lb.y));
+              float xa0, xa1, p2, p3;
+              f2unpack(xa, xa0, xa1);
+              const float p0 = exp2_mufu(xa0), p1 = exp2_mufu(xa1);
+              exp2_poly2(xb, p2, p3);
+              const uint64_t pa = f2pack(p0, p1), pb = f2pack(p2, p3);
+              const uint64_t dsa =
+                  f2mul(pa, f2sub(f2pack(__uint_as_float(dp[c0]), __uint_as_float(dp[c0 + 1])), f2pack(da.x, da.y)));
+              const uint64_t dsb = f2mul(
+                  pb, f2sub(f2pack(__uint_as_float(dp[c0 + 2]), __uint_as_float(dp[c0 + 3])), f2pack(db.x, db.y)));
+              float d0, d1, d2, d3;
+              f2unpack(dsa, d0, d1);
+              f2unpack(dsb, d2, d3);
+              pk[2 * h] = pack_bf16x2(p0, p1);
+              pk[2 * h + 1] = pack_bf16x2(p2, p3);
+              dk4[2 * h] = pack_bf16x2(d0, d1);
+              dk4[2 * h + 1] = pack_bf16x2(d2, d3);
             }
-            pk[i2p] = pack_bf16x2(pe[0], pe[1]);
-            dk4[i2p] = pack_bf16x2(de[0], de[1]);
+            *reinterpret_cast<uint4*>(panelP + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4*>(panelS + r * 128 + ((ch ^ (r & 7)) << 4)) =
+                make_uint4(dk4[0], dk4[1], dk4[2], dk4[3]);
           }
-          *reinterpret_cast<uint4*>(panelP + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          *reinterpret_cast<uint4*>(panelS + r * 128 + ((ch ^ (r & 7)) << 4)) =
-              make_uint4(dk4[0], dk4[1], dk4[2], dk4[3]);
+        } else {
+  #pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            uint32_t pk[4], dk4[4];
+  #pragma unroll
+            for (int i2p = 0; i2p < 4; ++i2p) {
+              float pe[2], de[2];
+  #pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int col = ch * 8 + i2p * 2 + e;
+                const int qi = qbase + col;
+                float pv = 0.f, ds = 0.f;
+                if (key_ok && qi < p.Nq) {
+                  pv = exp2_mufu(fmaf(__uint_as_float(sv[col]), p.scale_log2, sl[col]));
+                  ds = pv * (__uint_as_float(dp[col]) - sd[col]);
+                }
+                pe[e] = pv;
+                de[e] = ds;
+              }
+              pk[i2p] = pack_bf16x2(pe[0], pe[1]);
+              dk4[i2p] = pack_bf16x2(de[0], de[1]);
+            }
+            *reinterpret_cast<uint4*>(panelP + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4*>(panelS + r * 128 + ((ch ^ (r & 7)) << 4)) =
+                make_uint4(dk4[0], dk4[1], dk4[2], dk4[3]);
+          }
         }
         fence_proxy_async_smem();
         tc_fence_before();
