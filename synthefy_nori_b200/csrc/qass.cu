@@ -48,8 +48,16 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
 }
 
 __device__ __forceinline__ float gelu(float z) { return 0.5f * z * (1.0f + erff(z * 0.70710678118654752f)); }
-__device__ __forceinline__ float gelu_grad(float z) {
-  return 0.5f * (1.0f + erff(z * 0.70710678118654752f)) + z * 0.3989422804014327f * expf(-0.5f * z * z);
+// tanh(x) = 1 - 2 / (1 + e^(2x)) with the fast exponential and division intrinsics: absolute
+// error ~1e-7 (the gate only uses 1 + tanh and 1 - tanh^2, where that is far below bf16
+// resolution); saturates to +-1 for large |x|.
+__device__ __forceinline__ float tanh_fast(float x) { return 1.0f - __fdividef(2.0f, 1.0f + __expf(2.0f * x)); }
+
+// gelu(z) and gelu'(z) from one erf evaluation (the backward needs both)
+__device__ __forceinline__ void gelu_and_grad(float z, float& g, float& dg) {
+  const float cdf = 0.5f * (1.0f + erff(z * 0.70710678118654752f));
+  g = z * cdf;
+  dg = cdf + z * 0.3989422804014327f * __expf(-0.5f * z * z);
 }
 
 // A fragments of a [16 x 64] bf16 tile (rows = vectors) stored swizzled at `tile`.
@@ -265,7 +273,7 @@ __global__ void __launch_bounds__(kThreads) qass_fwd_kernel(Params p) {
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) t[i][e] = 1.0f + tanhf(t[i][e]);
+        for (int e = 0; e < 4; ++e) t[i][e] = 1.0f + tanh_fast(t[i][e]);
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) t[i][0] = t[i][1] = t[i][2] = t[i][3] = 1.0f;
@@ -363,7 +371,12 @@ __global__ void __launch_bounds__(kThreads) qass_bwd_kernel(Params p) {
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) act[i][e] = gelu(z1[i][e]);
+        for (int e = 0; e < 4; ++e) {
+          float g, dg;
+          gelu_and_grad(z1[i][e], g, dg);
+          act[i][e] = g;
+          z1[i][e] = dg;  // z1 is only needed through gelu'(z1) from here on
+        }
       uint32_t aa[4][4];
       acc_to_a(act, aa);
       mma_nt(z2, aa, sW2, lane);
@@ -389,7 +402,7 @@ __global__ void __launch_bounds__(kThreads) qass_bwd_kernel(Params p) {
             x = __bfloat162float(*qt);
           }
           const float sv = ss[h * 64 + (d < 64 ? d : 0)];
-          const float t = p.gate ? tanhf(z2[i][e]) : 0.f;
+          const float t = p.gate ? tanh_fast(z2[i][e]) : 0.f;
           const float gate = 1.0f + t;
           dqd[i][e] = dqp * gate * sv;
           if (ok && d < p.D) {
@@ -433,7 +446,7 @@ __global__ void __launch_bounds__(kThreads) qass_bwd_kernel(Params p) {
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) dz1[i][e] = dh[i][e] * gelu_grad(z1[i][e]);
+        for (int e = 0; e < 4; ++e) dz1[i][e] = dh[i][e] * z1[i][e];  // z1 holds gelu'(z1)
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         float s0 = dz1[i][0] + dz1[i][2], s1 = dz1[i][1] + dz1[i][3];
