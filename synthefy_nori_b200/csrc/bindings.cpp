@@ -42,7 +42,7 @@ torch::Tensor qass_bwd(const torch::Tensor& q, const torch::Tensor& dout, const 
                        const c10::optional<torch::Tensor>& w2, const c10::optional<torch::Tensor>& b2,
                        torch::Tensor& gs, const c10::optional<torch::Tensor>& gw1,
                        const c10::optional<torch::Tensor>& gb1, const c10::optional<torch::Tensor>& gw2,
-                       const c10::optional<torch::Tensor>& gb2, int64_t H, int64_t D);
+                       const c10::optional<torch::Tensor>& gb2, int64_t H, int64_t D, const c10::optional<torch::Tensor>& out);
 void peer_ddp_step(std::vector<int64_t> grads, std::vector<int64_t> params, std::vector<int64_t> flags,
                    std::vector<int64_t> norms, int64_t rank, int64_t s0, int64_t s1, const torch::Tensor& bounds,
                    int64_t step, torch::Tensor& red, torch::Tensor& m, torch::Tensor& v,

@@ -630,7 +630,8 @@ torch::Tensor qass_bwd(const torch::Tensor& q, const torch::Tensor& dout, const 
                        const c10::optional<torch::Tensor>& w2, const c10::optional<torch::Tensor>& b2,
                        torch::Tensor& gs, const c10::optional<torch::Tensor>& gw1,
                        const c10::optional<torch::Tensor>& gb1, const c10::optional<torch::Tensor>& gw2,
-                       const c10::optional<torch::Tensor>& gb2, int64_t H, int64_t D) {
+                       const c10::optional<torch::Tensor>& gb2, int64_t H, int64_t D,
+                       const c10::optional<torch::Tensor>& out) {
   check_q(q, H, D);
   TORCH_CHECK(dout.scalar_type() == at::kFloat && dout.dim() == 2 && dout.stride(1) == 1 && dout.size(0) == q.size(0),
               "qass_bwd: fp32 [R, H*D] gradient");
@@ -638,7 +639,16 @@ torch::Tensor qass_bwd(const torch::Tensor& q, const torch::Tensor& dout, const 
   TORCH_CHECK(dout.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(dout.data_ptr()) % 16 == 0,
               "qass_bwd: gradient rows must be 16-byte aligned");
   const at::cuda::CUDAGuard guard(q.device());
-  auto dq = torch::empty({q.size(0), H * D}, q.options());
+  torch::Tensor dq;
+  if (out.has_value() && out->defined()) {  // written in place (e.g. a column block of a wider gradient)
+    dq = *out;
+    TORCH_CHECK(dq.scalar_type() == at::kBFloat16 && dq.dim() == 2 && dq.size(0) == q.size(0) &&
+                    dq.size(1) == H * D && dq.stride(1) == 1 && dq.stride(0) % 2 == 0 &&
+                    reinterpret_cast<uintptr_t>(dq.data_ptr()) % 4 == 0,
+                "qass_bwd: out must be bf16 [R, H*D] with unit column stride and 4-byte aligned rows");
+  } else {
+    dq = torch::empty({q.size(0), H * D}, q.options());
+  }
   qass::Params p{};
   p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
   p.ldq = q.stride(0);

@@ -203,9 +203,10 @@ def qass_fwd(q, s, w1=None, b1=None, w2=None, b2=None, *, H: int, D: int):
 
 
 def qass_bwd(q, dout, s, gs, w1=None, b1=None, w2=None, b2=None, gw1=None, gb1=None, gw2=None, gb2=None, *, H: int,
-             D: int):
-    """Backward of ``qass_fwd``: returns dq (bf16); accumulates ds and the gate-MLP grads."""
-    return _lib().qass_bwd(q, dout, s, w1, b1, w2, b2, gs, gw1, gb1, gw2, gb2, int(H), int(D))
+             D: int, out=None):
+    """Backward of ``qass_fwd``: returns dq (bf16; written into ``out`` when given, e.g. the
+    query columns of a fused Q/K/V gradient); accumulates ds and the gate-MLP grads."""
+    return _lib().qass_bwd(q, dout, s, w1, b1, w2, b2, gs, gw1, gb1, gw2, gb2, int(H), int(D), out)
 
 
 def quantile_decode(pred: torch.Tensor, taus: torch.Tensor, levels=None, return_sorted: bool = False):

@@ -243,8 +243,7 @@ class SeqSublayer(torch.autograd.Function):
         qp_self, qp_cross = list(qparams[:8]), list(qparams[8:])
         grads_qp = [None] * len(qparams)
         if qmode:
-            dq_raw, gq = _qass_backward(qp_self, qmode, y_ctx[:, :E], g.ep, g, dq_self)
-            dy_ctx[:, :E] = dq_raw
+            _, gq = _qass_backward(qp_self, qmode, y_ctx[:, :E], g.ep, g, dq_self, out=dy_ctx[:, :E])
             grads_qp[:8] = gq
         else:
             dy_ctx[:, :E] = dq_self
@@ -277,9 +276,10 @@ class SeqSublayer(torch.autograd.Function):
                 None, *grads_qp)
 
 
-def _qass_backward(params, mode, q_raw, n_keys, g: Geometry, dq_out):
-    """Gradients of the QASS rescale w.r.t. the raw query (bf16) and the eight QASS
-    parameters (base MLP through the base scale, gate MLP from the fused kernel)."""
+def _qass_backward(params, mode, q_raw, n_keys, g: Geometry, dq_out, out=None):
+    """Gradients of the QASS rescale w.r.t. the raw query (bf16, written into ``out`` when
+    given) and the eight QASS parameters (base MLP through the base scale, gate MLP from
+    the fused kernel)."""
     H, D = g.H, g.D
     dev = q_raw.device
     base = [p.detach().requires_grad_(True) if p is not None else None for p in params[:4]]
@@ -292,10 +292,10 @@ def _qass_backward(params, mode, q_raw, n_keys, g: Geometry, dq_out):
         gw1, gb1 = torch.zeros_like(g1w, dtype=torch.float32), torch.zeros_like(g1b, dtype=torch.float32)
         gw2, gb2 = torch.zeros_like(g2w, dtype=torch.float32), torch.zeros_like(g2b, dtype=torch.float32)
         dq = ops.qass_bwd(q_raw, dq_out, s.detach(), gs, g1w.detach(), g1b.detach(), g2w.detach(), g2b.detach(), gw1,
-                          gb1, gw2, gb2, H=H, D=D)
+                          gb1, gw2, gb2, H=H, D=D, out=out)
         gate_grads = [gw1, gb1, gw2, gb2]
     else:
-        dq = ops.qass_bwd(q_raw, dq_out, s.detach(), gs, H=H, D=D)
+        dq = ops.qass_bwd(q_raw, dq_out, s.detach(), gs, H=H, D=D, out=out)
         gate_grads = [None] * 4
     if mode == "log_only" or base[0] is None:
         base_grads = [None] * 4

@@ -48,3 +48,8 @@ def test_qass_fused_matches_torch(mode, H, D):
         assert gk is not None
         cos = torch.nn.functional.cosine_similarity(gk.flatten().double(), p.grad.flatten().double(), dim=0)
         assert cos > 0.99, (p.shape, float(cos))
+    # the same gradient written in place into a column block of a wider buffer
+    wide = torch.zeros(R, 3 * E, device="cuda", dtype=torch.bfloat16)
+    _qass_backward(params, mode, q, 777, g, dq_out, out=wide[:, E:2 * E])
+    assert torch.equal(wide[:, E:2 * E], dq)
+    assert wide[:, :E].abs().max().item() == 0 and wide[:, 2 * E:].abs().max().item() == 0
