@@ -141,6 +141,15 @@ struct Params {
   int H, D, gate;
 };
 
+// vector index -> (token row, head) in 32-bit arithmetic (a 64-bit division is a long
+// software sequence on the GPU); the host checks R * H < 2^31
+__device__ __forceinline__ void vec_split(int64_t v, int H, int64_t& row, int& h) {
+  const unsigned vv = static_cast<unsigned>(v), hh = static_cast<unsigned>(H);
+  const unsigned rr = vv / hh;
+  row = rr;
+  h = static_cast<int>(vv - rr * hh);
+}
+
 // stage weights as bf16 swizzled [64][64]: W1 rows = hidden j (cols d), W2 rows = d (cols j)
 __device__ __forceinline__ void stage_weights(const Params& p, uint8_t* sW1, uint8_t* sW2, float* sb1, float* sb2,
                                               float* ss) {
@@ -168,8 +177,9 @@ __device__ __forceinline__ void load_q(const Params& p, int64_t v0, uint8_t* til
     const int64_t v = v0 + r;
     uint4 w = make_uint4(0u, 0u, 0u, 0u);
     if (v < p.R * p.H && c * 8 < p.D) {
-      const int64_t row = v / p.H;
-      const int h = static_cast<int>(v % p.H);
+      int64_t row;
+      int h;
+      vec_split(v, p.H, row, h);
       w = *reinterpret_cast<const uint4*>(p.q + row * p.ldq + h * p.D + c * 8);
     }
     *reinterpret_cast<uint4*>(tile + swz(r, c)) = w;
@@ -195,7 +205,10 @@ __device__ __forceinline__ void prefetch_q(const Params& p, int64_t v0, uint8_t*
     if (c >= nc) continue;
     const int64_t v = v0 + r;
     const bool ok = v < nvec;
-    const __nv_bfloat16* src = ok ? p.q + (v / p.H) * p.ldq + (v % p.H) * p.D + c * 8 : p.q;
+    int64_t row = 0;
+    int h = 0;
+    if (ok) vec_split(v, p.H, row, h);
+    const __nv_bfloat16* src = ok ? p.q + row * p.ldq + h * p.D + c * 8 : p.q;
     cp_async16(tile + swz(r, c), src, ok ? 16 : 0);
   }
 }
@@ -219,7 +232,10 @@ __device__ __forceinline__ void prefetch_dout(const Params& p, int64_t v0, float
     if (c >= nc) continue;
     const int64_t v = v0 + r;
     const bool ok = v < nvec;
-    const float* src = ok ? p.dout + (v / p.H) * p.ldd + (v % p.H) * p.D + c * 4 : p.dout;
+    int64_t row = 0;
+    int h = 0;
+    if (ok) vec_split(v, p.H, row, h);
+    const float* src = ok ? p.dout + row * p.ldd + h * p.D + c * 4 : p.dout;
     cp_async16(tile + r * kDoutLd + c * 4, src, ok ? 16 : 0);
   }
 }
@@ -282,8 +298,9 @@ __global__ void __launch_bounds__(kThreads) qass_fwd_kernel(Params p) {
     for (int half = 0; half < 2; ++half) {
       const int64_t v = v0 + g + half * 8;
       if (v >= nvec) continue;
-      const int64_t row = v / p.H;
-      const int h = static_cast<int>(v % p.H);
+      int64_t row;
+      int h;
+      vec_split(v, p.H, row, h);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int d = i * 8 + cc;
@@ -387,7 +404,9 @@ __global__ void __launch_bounds__(kThreads) qass_bwd_kernel(Params p) {
     for (int half = 0; half < 2; ++half) {
       const int64_t v = v0 + g + half * 8;
       const bool ok = v < nvec;
-      const int h = ok ? static_cast<int>(v % p.H) : 0;
+      int64_t row_unused = 0;
+      int h = 0;
+      if (ok) vec_split(v, p.H, row_unused, h);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
 #pragma unroll
@@ -478,8 +497,9 @@ __global__ void __launch_bounds__(kThreads) qass_bwd_kernel(Params p) {
     for (int half = 0; half < 2; ++half) {
       const int64_t v = v0 + g + half * 8;
       if (v >= nvec) continue;
-      const int64_t row = v / p.H;
-      const int h = static_cast<int>(v % p.H);
+      int64_t row;
+      int h;
+      vec_split(v, p.H, row, h);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int d = i * 8 + cc;
@@ -569,6 +589,7 @@ static void check_q(const torch::Tensor& q, int64_t H, int64_t D) {
               "qass: bf16 [R, >= H*D] row-major q");
   TORCH_CHECK(D > 0 && D <= 64 && D % 8 == 0 && q.size(1) >= H * D, "qass: head dim multiple of 8, <= 64");
   TORCH_CHECK(q.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0, "qass: 16-byte rows");
+  TORCH_CHECK(q.size(0) * H < 2147483647LL, "qass: at most 2^31 - 1 (row, head) vectors per call");
 }
 
 // q' = q * s * (1 + tanh(gate(q))) (gate optional) -> new [R, H*D] bf16
