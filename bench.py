@@ -1,14 +1,17 @@
 """Headline benchmark: nori-100m DDP pretraining throughput (tables/s, whole job).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload train|train30m|infer5|infer4|infer1]
 
 For N > 1 run under ``torch.distributed.run`` (one rank per GPU, NCCL, rendezvous on
-127.0.0.1).  Config (nori-100m training on the config-3 table shapes):
+127.0.0.1).  Headline config: nori-100m training on the pretraining table shapes:
 random-init nori-100m weights, synthetic SCM-prior tables, 16 tables per GPU per step
 (32, the nori-30m config's batch, does not fit the reference's nori-100m step in 180 GB),
 rows ~ U[512, 2048] (one row count per step, shared by the batch), context fraction
 ~ U[0.5, 0.9], features ~ U[5, 100] padded to 100, 999-quantile pinball loss (+0.05
 monotonicity), bf16 compute, clip 1.0, AdamW + EMA 0.999, activation checkpointing.
+``--workload train30m`` is the same with nori-30m and 32 tables per GPU, the config whose
+gradient exchange is largest relative to its compute (25 MB gradient buckets).
 
 ``value`` times W untimed warm-up steps then exactly K steps on the device (CUDA
 events, barrier + synchronize on both sides, max over ranks); each step generates its
@@ -20,9 +23,12 @@ pinned memory and the loss read back to the host.
 
 ``--impl reference`` runs the unmodified reference package from ``baseline/_ref``
 (its FeaturesTransformer with bf16 autocast, SDPA attention, native RMSNorm, layer
-checkpointing, ``compute_ccmm_loss`` pinball objective, torch AdamW, its EMA helper,
-DDP/NCCL for N > 1) on the same table shapes; its tables are generated before the
-timed region.
+checkpointing, the regional ``torch.compile`` of the encoder layer that its stock
+launcher enables (``--reference-compile none`` for eager; a compile failure falls back
+to eager and is reported), ``compute_ccmm_loss`` pinball objective, torch AdamW, its EMA
+helper, DDP/NCCL with 25 MB buckets for N > 1) on the same table shapes; its tables are
+generated before the timed region, and its ``e2e`` copies each step's tables from pinned
+host memory and reads the loss back, like ours.
 """
 
 from __future__ import annotations
@@ -45,7 +51,6 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-METRIC = "nori-100m train tables/s"
 
 
 def parse():
@@ -54,8 +59,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=6)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--model", default="nori-100m")
-    ap.add_argument("--tables-per-gpu", type=int, default=16)
+    ap.add_argument("--model", default=None, help="default: nori-100m (train), nori-30m (train30m)")
+    ap.add_argument("--tables-per-gpu", type=int, default=None, help="default: 16 (train), 32 (train30m)")
     ap.add_argument("--min-rows", type=int, default=512)
     ap.add_argument("--max-rows", type=int, default=2048)
     ap.add_argument("--features", type=int, default=100)
@@ -64,12 +69,23 @@ def parse():
     ap.add_argument("--grad-reduction", default="peer", choices=["nccl", "peer"],
                     help="N > 1: peer = in-kernel reduce-scatter / sharded AdamW / all-gather over NVLink peer memory; "
                          "nccl = all-reduce baseline")
-    ap.add_argument("--workload", default="train", choices=["train", "infer5", "infer4", "infer1"],
-                    help="train (headline), infer5 (batched multi-table cached inference, BASELINE config 5), "
-                         "infer4 (100k-row context, int8 KV, BASELINE config 4)")
+    ap.add_argument("--workload", default="train", choices=["train", "train30m", "infer5", "infer4", "infer1"],
+                    help="train (headline: nori-100m, 16 tables/GPU), train30m (nori-30m, 32 tables/GPU, the "
+                         "gradient-bound pretraining config), infer5 (256 tables x 2048 context rows, cached, "
+                         "4 query calls), infer4 (one 100k-row context, int8 KV, 10k queries), infer1 (nori-6m on CPU)")
+    ap.add_argument("--reference-compile", default="dynamic", choices=["dynamic", "none"],
+                    help="reference arm: regional torch.compile of the encoder layer as the reference's stock "
+                         "launcher enables it (dynamic), or eager (none); a compile failure falls back to eager "
+                         "and is reported in the JSON line")
+    ap.add_argument("--bucket-mb", type=float, default=25.0, help="peer DDP gradient bucket size (MB)")
     ap.add_argument("--infer-tables", type=int, default=256)
     ap.add_argument("--infer-group", type=int, default=8, help="tables per cache build / predict batch")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.model is None:
+        args.model = "nori-30m" if args.workload == "train30m" else "nori-100m"
+    if args.tables_per_gpu is None:
+        args.tables_per_gpu = 32 if args.workload == "train30m" else 16
+    return args
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -182,7 +198,7 @@ def run_ours(args, device, world, rank):
         raise RuntimeError(f"native extension not loaded: {ops.native_import_error()}")
     torch.manual_seed(args.seed)
     model = build_model(preset_config(args.model))
-    trainer = NoriTrainer(model, TrainConfig(grad_reduction=args.grad_reduction), device)
+    trainer = NoriTrainer(model, TrainConfig(grad_reduction=args.grad_reduction, bucket_mb=args.bucket_mb), device)
     pc = prior_cfg(args)
     B = args.tables_per_gpu
     shapes = step_shapes(args, args.warmup + args.steps + 1)
@@ -201,35 +217,38 @@ def run_ours(args, device, world, rank):
     launches = count_native_launches(lambda: one(args.warmup + args.steps)) * args.steps
     ops.check_status(device)
     e2e = None if args.no_e2e else run_e2e(args, trainer, shapes, device, world, rank)
-    return ms, clk, launches, e2e, float(losses[-1].item())
+    info = {}
+    if trainer.peer is not None:
+        info["grad_buckets"] = trainer.peer.describe()
+    return ms, clk, launches, e2e, float(losses[-1].item()), info
 
 
 def run_e2e(args, trainer, shapes, device, world, rank):
-    """Public-API training from pinned host tables: H2D copy + train_step + loss.item()."""
-    from synthefy_nori_b200.training.prior import scm_prior_batch
+    """Public-API training from pinned host tables: H2D copy + ``NoriTrainer.train_step`` +
+    ``loss.item()`` per step."""
+    return _e2e_loop(args, trainer.train_step, shapes, device, world, rank)
 
-    pc = prior_cfg(args)
-    B = args.tables_per_gpu
-    host = []
-    # the same step shapes as the device-timed steps (shapes[warmup:warmup+steps]), plus one warm-up
-    for i in range(args.steps + 1):
-        rows, ep = shapes[args.warmup + i]
-        b = scm_prior_batch(pc, B, rows, ep, seed=args.seed * 7 + i + 100 * rank, device=device)
-        host.append((b.x.cpu().pin_memory(), b.y.cpu().pin_memory(), ep))
-    torch.cuda.synchronize(device)
 
-    def one(i):
-        x_h, y_h, ep = host[i]
-        x = x_h.to(device, non_blocking=True)
-        y = y_h.to(device, non_blocking=True)
-        return float(trainer.train_step(x, y, ep).item())
+def _compile_reference_layers(model):
+    """The reference launcher's default execution speedup: one ``torch.compile`` of the
+    encoder layer's forward (dynamic shapes) shared by every layer (reference
+    ``training/cli.py:1371-1397``, enabled by ``scripts/train.sh:30-35``)."""
+    import types
 
-    one(args.steps)  # warm
-    ms = timed(lambda: [one(i) for i in range(args.steps)], device, world)
-    h2d = sum(host[i][0].numel() * 4 + host[i][1].numel() * 4 for i in range(args.steps)) / args.steps
-    tables = B * world * args.steps
-    return {"value": tables / (ms / 1000.0), "unit": "tables/s", "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": 4, "ms_per_step": ms / args.steps}
+    for name in ("cache_size_limit", "recompile_limit", "accumulated_cache_size_limit",
+                 "accumulated_recompile_limit"):
+        if hasattr(torch._dynamo.config, name):
+            setattr(torch._dynamo.config, name, 1024)
+    torch._dynamo.config.optimize_ddp = False
+    layers = model.transformer_encoder.layers
+    compiled = torch.compile(type(layers[0]).forward, dynamic=True, fullgraph=False)
+    for layer in layers:
+        layer.forward = types.MethodType(compiled, layer)
+
+
+def _uncompile_reference_layers(model):
+    for layer in model.transformer_encoder.layers:
+        layer.__dict__.pop("forward", None)
 
 
 def run_reference(args, device, world, rank):
@@ -253,27 +272,31 @@ def run_reference(args, device, world, rank):
         if isinstance(m, RefRMSNorm):
             m.use_native = True
     model._skip_feature_decoder = True  # feature loss weight 0 (cli.py:1344-1350)
+    compile_state = "none"
+    if args.reference_compile == "dynamic":
+        _compile_reference_layers(model)
+        compile_state = "dynamic regional (encoder layer)"
     model.transformer_encoder.gradient_checkpointing = True
     model.train()
     net = model
     if world > 1:
         from torch.nn.parallel import DistributedDataParallel as DDP
 
-        net = DDP(model, device_ids=[device.index], find_unused_parameters=False, gradient_as_bucket_view=True)
+        net = DDP(model, device_ids=[device.index], find_unused_parameters=False, gradient_as_bucket_view=True,
+                  bucket_cap_mb=args.bucket_mb)
     params = [p for p in model.parameters() if p.requires_grad]
     opt = torch.optim.AdamW(params, lr=3e-4, betas=(0.9, 0.95), weight_decay=0.01)
     ema = {k: v.detach().clone() for k, v in model.state_dict().items()}
     quantiles = list(model.regression_quantiles)
     pc = prior_cfg(args)
     B = args.tables_per_gpu
-    shapes = step_shapes(args, args.warmup + args.steps)
+    shapes = step_shapes(args, args.warmup + args.steps + 1)
     batches = []
-    for i, (rows, ep) in enumerate(shapes):
+    for i, (rows, ep) in enumerate(shapes[: args.warmup + args.steps]):
         b = scm_prior_batch(pc, B, rows, ep, seed=args.seed * 1000003 + i * 7919 + rank, device=device)
         batches.append((b.x, b.y, ep))
 
-    def one(i):
-        x, y, ep = batches[i]
+    def step(x, y, ep):
         opt.zero_grad(set_to_none=True)
         with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
             out = net(x=x, y=y[:, :ep], eval_pos=ep, task_type="reg")
@@ -286,13 +309,72 @@ def run_reference(args, device, world, rank):
         _foreach_ema_update(ema, model.state_dict(), 0.999)
         return loss.detach()
 
+    def one(i):
+        return step(*batches[i])
+
+    # warm-up; with regional compile the first shapes also compile (static, then dynamic).
+    # Every rank takes the same branch: a compile failure on any rank turns compile off on all.
+    failed = None
     for i in range(args.warmup):
-        one(i)
+        try:
+            one(i)
+            err = 0
+        except Exception as exc:  # noqa: BLE001 - Inductor / Dynamo failures surface here
+            if compile_state == "none":
+                raise
+            failed, err = f"{type(exc).__name__}: {str(exc).splitlines()[0][:160]}", 1
+        flag = torch.tensor([err], device=device)
+        if world > 1:
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        if int(flag.item()) and compile_state != "none":
+            _uncompile_reference_layers(model)
+            compile_state = f"none (regional compile failed: {failed or 'on another rank'})"
+            opt.zero_grad(set_to_none=True)
+            torch.cuda.synchronize(device)
+            one(i)
     clocks = ClockSampler(device)
     losses = []
     ms = timed(lambda: [losses.append(one(args.warmup + i)) for i in range(args.steps)], device, world)
     clk = clocks.stop()
-    return ms, clk, 0, None, float(losses[-1].item())
+    del batches
+    e2e = None
+    if not args.no_e2e:
+        e2e = _e2e_loop(args, step, shapes, device, world, rank)
+    return ms, clk, 0, e2e, float(losses[-1].item()), {"reference_compile": compile_state}
+
+
+def _host_batches(args, shapes, device, rank):
+    """Pinned host copies of the tables for the end-to-end loop (the device-timed steps'
+    shapes plus one warm-up table set), generated before the timed region."""
+    from synthefy_nori_b200.training.prior import scm_prior_batch
+
+    pc = prior_cfg(args)
+    host = []
+    for i in range(args.steps + 1):
+        rows, ep = shapes[args.warmup + i]
+        b = scm_prior_batch(pc, args.tables_per_gpu, rows, ep, seed=args.seed * 7 + i + 100 * rank, device=device)
+        host.append((b.x.cpu().pin_memory(), b.y.cpu().pin_memory(), ep))
+    torch.cuda.synchronize(device)
+    return host
+
+
+def _e2e_loop(args, step, shapes, device, world, rank):
+    """End to end through a step callable: every step copies its tables host->device from
+    pinned memory and reads the loss back to the host inside the timed region."""
+    host = _host_batches(args, shapes, device, rank)
+
+    def one(i):
+        x_h, y_h, ep = host[i]
+        x = x_h.to(device, non_blocking=True)
+        y = y_h.to(device, non_blocking=True)
+        return float(step(x, y, ep).item())
+
+    one(args.steps)  # warm
+    ms = timed(lambda: [one(i) for i in range(args.steps)], device, world)
+    h2d = sum(host[i][0].numel() * 4 + host[i][1].numel() * 4 for i in range(args.steps)) / args.steps
+    tables = args.tables_per_gpu * world * args.steps
+    return {"value": tables / (ms / 1000.0), "unit": "tables/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": 4, "ms_per_step": ms / args.steps}
 
 
 # ----------------------------------------------------------------------------- inference
@@ -314,7 +396,7 @@ def _infer_tables(n_tables, n_ctx, n_q, n_feat, seed, device, nan_frac=0.15, n_c
 
 
 def run_infer5(args, device, world, rank, impl):
-    """tables data-parallel over ranks; per group of tables the context
+    """Batched multi-table cached inference: tables data-parallel over ranks; per group of tables the context
     cache is built once, then 4 predict calls with 512 fresh query rows each (timed)."""
     n_ctx, n_feat, n_q, calls = 2048, 50, 512, 4
     per_rank = args.infer_tables // world
@@ -366,7 +448,7 @@ def run_infer5(args, device, world, rank, impl):
 
 
 def run_infer4(args, device, world, rank, impl):
-    """BASELINE config 4 on one GPU: one table, 100k context rows x 100 features (20
+    """Long-context inference: one table, 100k context rows x 100 features (20
     categorical), int8 KV cache, 10k query rows; build + query timed separately."""
     n_ctx = int(os.environ.get("NORI_INFER4_CTX", "100000"))
     n_q = int(os.environ.get("NORI_INFER4_QUERY", "10000"))
@@ -433,7 +515,7 @@ def run_infer4(args, device, world, rank, impl):
 
 
 def run_infer1(args, impl):
-    """BASELINE config 1: nori-6m single-table inference on the CPU (512 context rows x 10
+    """nori-6m single-table inference on the CPU (512 context rows x 10
     features, 5% NaN, y = Xw + 0.5 sin(3 x0) + N(0, 0.1^2); 128 query rows; the mean plus
     quantiles 0.1 / 0.5 / 0.9).  Wall-clock latency per call (the CPU has no device timer),
     median over the timed calls, one model forward per call (no ensemble)."""
@@ -519,7 +601,7 @@ def main():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
     t0 = time.time()
-    if args.workload != "train":
+    if not args.workload.startswith("train"):
         main_infer(args, device, world, rank)
         if world > 1:
             dist.barrier()
@@ -533,12 +615,20 @@ def main():
             return
     else:
         res = run_ours(args, device, world, rank)
-    ms, clk, launches, e2e, last_loss = res
+    ms, clk, launches, e2e, last_loss, info = res
     tables = args.tables_per_gpu * world * args.steps
     value = tables / (ms / 1000.0)
     if rank == 0:
+        if world == 1:
+            reduction = "none (one GPU)"
+        elif args.impl == "reference":
+            reduction = f"DDP/NCCL all-reduce, {args.bucket_mb:g} MB buckets"
+        elif args.grad_reduction == "peer":
+            reduction = f"peer-memory reduce-scatter over NVLink, {args.bucket_mb:g} MB buckets overlapped with backward"
+        else:
+            reduction = "NCCL all-reduce"
         line = {
-            "metric": METRIC,
+            "metric": f"{args.model} train tables/s",
             "value": round(value, 3),
             "unit": "tables/s",
             "n_gpus": world,
@@ -559,14 +649,15 @@ def main():
                 "loss": "pinball 999 + 0.05 monotonicity",
                 "optimizer": "AdamW + EMA 0.999, clip 1.0",
                 "l2": "per-step working set is several GB (> 126 MB L2); no flush needed",
-                "grad_reduction": args.grad_reduction if args.impl == "ours" else "DDP/NCCL",
             },
+            "grad_reduction": reduction,
             "clocks": clk,
             "gpu_launches": launches,
             "peak_mem_gib": round(torch.cuda.max_memory_allocated(device) / 2 ** 30, 1),
             "last_loss": last_loss,
             "wall_s": round(time.time() - t0, 1),
         }
+        line.update(info)
         if args.impl == "reference":
             line["impl"] = "reference"
         if e2e is not None:

@@ -56,9 +56,9 @@ class NoriCausal(BaseEstimator):
         if self.network is not None:
             return self.network.to(device).eval(), None
         from synthefy_nori_b200.causal.network import NoriCausalNetwork
-        from synthefy_nori_b200.causal.registry import get_checkpoint_path_and_threshold
+        from synthefy_nori_b200.causal.registry import resolve_causal_checkpoint
 
-        path, thr = get_checkpoint_path_and_threshold(self.model, self.checkpoint)
+        path, thr = resolve_causal_checkpoint(self.model, self.checkpoint)
         key = (str(path), str(device))
         if key not in _NETWORKS:
             _NETWORKS[key] = NoriCausalNetwork.from_checkpoint(path, device)[0]

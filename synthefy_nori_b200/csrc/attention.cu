@@ -1179,14 +1179,32 @@ extern "C" __attribute__((visibility("default"))) cudaError_t nori_attention_bwd
     const int64_t* ldk, const int64_t* ldv, int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid, double scale,
     cudaStream_t stream) {
   g_noalloc_error.clear();
+  // Every check runs before anything is queued: a rejected call changes nothing.
   if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv || !lq || !lk || !lv || !lo || !ldo || !ldk || !ldv)
     return noalloc_fail("nori_attention_bwd_noalloc: null pointer argument");
   if (BH < 0 || Nq < 0 || Nk < 0) return noalloc_fail("nori_attention_bwd_noalloc: negative size");
-  if (BH * Nq > static_cast<int64_t>(NORI_NOALLOC_MAX_ROWS))
+  const int64_t kMax = static_cast<int64_t>(NORI_NOALLOC_MAX_ROWS);
+  if (BH > kMax || Nq > kMax || BH * Nq > kMax)  // each factor bounded first: the product cannot overflow
     return noalloc_fail("nori_attention_bwd_noalloc: BH * Nq exceeds NORI_NOALLOC_MAX_ROWS (1048576)");
+  if (Nk > 2147483647LL) return noalloc_fail("nori_attention_bwd_noalloc: Nk too large");
   if (d_valid <= 0 || d_valid > nori::kD || d_valid % 8 != 0)
     return noalloc_fail("nori_attention_bwd_noalloc: head dim must be a multiple of 8, at most 64");
+  // the kernels move bf16 rows in 16-byte vectors and dq in float4s
+  for (const void* ptr : {q, k, v, o, dout, static_cast<const void*>(dq), static_cast<const void*>(dk),
+                          static_cast<const void*>(dv)})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+      return noalloc_fail("nori_attention_bwd_noalloc: q, k, v, o, dout, dq, dk and dv must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(lse) % 4 != 0)
+    return noalloc_fail("nori_attention_bwd_noalloc: lse must be 4-byte aligned");
+  for (const int64_t* l : {lq, lk, lv, lo, ldo, ldk, ldv}) {
+    if (l[0] < 0 || l[1] < 0 || l[2] < 0 || l[3] < 0 || l[0] % 8 || l[1] % 8 || l[2] % 8 || l[3] % 8)
+      return noalloc_fail("nori_attention_bwd_noalloc: layout strides must be non-negative multiples of 8 elements");
+    if (l[4] <= 0 || l[5] <= 0 || l[4] > 2147483647LL || l[5] > 2147483647LL)
+      return noalloc_fail("nori_attention_bwd_noalloc: layout d1 and d2 must be positive and fit in 32 bits");
+  }
   if (BH == 0 || Nq == 0 || Nk == 0) return cudaSuccess;
+  const int64_t n_tiles_k = (Nk + nori::kBlkK - 1) / nori::kBlkK;
+  if (BH * n_tiles_k >= 2147483647LL) return noalloc_fail("nori_attention_bwd_noalloc: grid too large");
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
@@ -1237,8 +1255,7 @@ extern "C" __attribute__((visibility("default"))) cudaError_t nori_attention_bwd
   p.q_d_valid = p.d_valid;
   p.scale = static_cast<float>(scale);
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
-  p.n_tiles_k = static_cast<int>((Nk + nori::kBlkK - 1) / nori::kBlkK);
-  if (BH * p.n_tiles_k >= 2147483647LL) return noalloc_fail("nori_attention_bwd_noalloc: grid too large");
+  p.n_tiles_k = static_cast<int>(n_tiles_k);
   nori::attn_bwd_kernel<<<static_cast<unsigned>(BH * p.n_tiles_k), nori::kAttnThreads, 0, stream>>>(p);
   return cudaGetLastError();
 }

@@ -1152,4 +1152,23 @@ void attn_bwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Element-wise exp2_poly over a tensor: lets the tests check the softmax's FMA-pipe
+// exponential against CUDA's exp2f over its whole input range.
+__global__ void exp2_poly_eval_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = exp2_poly(x[i]);
+}
+
+torch::Tensor exp2_poly_eval(const torch::Tensor& x) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.is_contiguous(), "exp2_poly_eval: fp32 CUDA tensor");
+  const at::cuda::CUDAGuard guard(x.device());
+  auto y = torch::empty_like(x);
+  const int64_t n = x.numel();
+  if (n == 0) return y;
+  exp2_poly_eval_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      x.data_ptr<float>(), y.data_ptr<float>(), n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return y;
+}
+
 }  // namespace nori

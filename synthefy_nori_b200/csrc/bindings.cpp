@@ -9,7 +9,7 @@ torch::Tensor gemm_swiglu(const torch::Tensor& A, const torch::Tensor& W, const 
                           const torch::Tensor& status, int64_t bn);
 torch::Tensor gemm_residual(const torch::Tensor& A, const torch::Tensor& W, const torch::Tensor& resid, double alpha,
                             const c10::optional<torch::Tensor>& sumsq, const torch::Tensor& status, int64_t bn,
-                            const c10::optional<torch::Tensor>& out_opt);
+                            const c10::optional<torch::Tensor>& out_opt, bool w_kn);
 void gemm_wgrad(const torch::Tensor& dY, const torch::Tensor& X, torch::Tensor& out, const torch::Tensor& status,
                 int64_t bn, int64_t splits, double alpha);
 torch::Tensor rms_apply(const torch::Tensor& x, const torch::Tensor& rs);
@@ -43,12 +43,22 @@ torch::Tensor qass_bwd(const torch::Tensor& q, const torch::Tensor& dout, const 
                        torch::Tensor& gs, const c10::optional<torch::Tensor>& gw1,
                        const c10::optional<torch::Tensor>& gb1, const c10::optional<torch::Tensor>& gw2,
                        const c10::optional<torch::Tensor>& gb2, int64_t H, int64_t D, const c10::optional<torch::Tensor>& out);
-void peer_ddp_step(std::vector<int64_t> grads, std::vector<int64_t> params, std::vector<int64_t> flags,
-                   std::vector<int64_t> norms, int64_t rank, int64_t s0, int64_t s1, const torch::Tensor& bounds,
-                   int64_t step, torch::Tensor& red, torch::Tensor& m, torch::Tensor& v,
-                   const c10::optional<torch::Tensor>& ema, torch::Tensor& local_norm, double lr, double beta1,
-                   double beta2, double eps, double wd, int64_t opt_step, double ema_decay, double max_norm,
-                   double grad_scale, const torch::Tensor& status);
+torch::Tensor exp2_poly_eval(const torch::Tensor& x);
+void peer_wait(int64_t flags, int64_t base, int64_t W, int64_t step, double limit_s, const torch::Tensor& status);
+void peer_signal(std::vector<int64_t> flags, int64_t rank, int64_t slot, int64_t step);
+void peer_bucket_pack_signal(int64_t grad, int64_t wire, int64_t b0, int64_t n, int64_t counter,
+                             std::vector<int64_t> flags, int64_t rank, int64_t slot, int64_t step, int64_t device);
+void peer_bucket_reduce(std::vector<int64_t> wire, int64_t f0, int64_t n, bool wire_bf16, double scale, int64_t red,
+                        int64_t norm_acc, const torch::Tensor& status, int64_t ctas);
+void peer_publish(std::vector<int64_t> flags, std::vector<int64_t> xchg, int64_t rank, int64_t local_norm,
+                  int64_t local_bits, int64_t slot, int64_t step);
+void peer_adamw(std::vector<int64_t> params, std::vector<int64_t> xchg, int64_t rank, const torch::Tensor& tab,
+                torch::Tensor& red, torch::Tensor& m, torch::Tensor& v, const c10::optional<torch::Tensor>& ema,
+                double lr, double beta1, double beta2, double eps, double wd, int64_t opt_step, double ema_decay,
+                double max_norm, int64_t max_piece, const torch::Tensor& diag, const torch::Tensor& status);
+void layout_sync(const torch::Tensor& seg, const torch::Tensor& chunks, std::vector<int64_t> params, int64_t rank,
+                 const c10::optional<torch::Tensor>& bstart, const c10::optional<torch::Tensor>& bper,
+                 const torch::Tensor& status);
 int64_t peer_malloc(int64_t bytes);
 void peer_free(int64_t ptr);
 torch::Tensor peer_ipc_handle(int64_t ptr);
@@ -80,7 +90,7 @@ void grad_sumsq(const torch::Tensor& g, torch::Tensor& out);
 void adamw_ema(torch::Tensor& p, const torch::Tensor& g, torch::Tensor& m, torch::Tensor& v,
                const c10::optional<torch::Tensor>& ema, const c10::optional<torch::Tensor>& pbf,
                const c10::optional<torch::Tensor>& norm_sq, double lr, double beta1, double beta2, double eps,
-               double wd, int64_t step, double ema_decay, double max_norm, double grad_scale);
+               double wd, int64_t step, double ema_decay, double max_norm, double grad_scale, const c10::optional<torch::Tensor>& skip);
 std::vector<torch::Tensor> quantize_int8(const torch::Tensor& x);
 void dequantize_int8(const torch::Tensor& q, const torch::Tensor& scale, torch::Tensor& out);
 }  // namespace nori
@@ -101,7 +111,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("copy_rows", &nori::copy_rows);
   m.def("rms_scale", &nori::rms_scale);
   m.def("quantile_decode", &nori::quantile_decode);
-  m.def("peer_ddp_step", &nori::peer_ddp_step);
+  m.def("exp2_poly_eval", &nori::exp2_poly_eval);
+  m.def("peer_wait", &nori::peer_wait);
+  m.def("peer_signal", &nori::peer_signal);
+  m.def("peer_bucket_pack_signal", &nori::peer_bucket_pack_signal);
+  m.def("peer_bucket_reduce", &nori::peer_bucket_reduce);
+  m.def("peer_publish", &nori::peer_publish);
+  m.def("peer_adamw", &nori::peer_adamw);
+  m.def("layout_sync", &nori::layout_sync);
   m.def("peer_malloc", &nori::peer_malloc);
   m.def("peer_free", &nori::peer_free);
   m.def("peer_ipc_handle", &nori::peer_ipc_handle);

@@ -514,28 +514,36 @@ torch::Tensor gemm_swiglu(const torch::Tensor& A, const torch::Tensor& W, const 
   return out;
 }
 
-// out = bf16(resid + alpha * (A @ W^T)); sumsq[m] += sum_n out[m, n]^2 (if given)
+// out = bf16(resid + alpha * (A @ W^T)); sumsq[m] += sum_n out[m, n]^2 (if given).
+// W is [N, K], or with w_kn the same matrix stored [K, N] (an MN-major operand: the
+// output projections read their [E_in, E_out] weights in place, no transposed copy).
 torch::Tensor gemm_residual(const torch::Tensor& A, const torch::Tensor& W, const torch::Tensor& resid, double alpha,
                             const c10::optional<torch::Tensor>& sumsq, const torch::Tensor& status, int64_t bn,
-                            const c10::optional<torch::Tensor>& out_opt) {
+                            const c10::optional<torch::Tensor>& out_opt, bool w_kn) {
   check_operand(A, "A");
   check_operand(W, "W");
   check_operand(resid, "resid");
-  TORCH_CHECK(A.size(1) == W.size(1), "gemm_residual: K mismatch");
-  TORCH_CHECK(resid.size(0) == A.size(0) && resid.size(1) == W.size(0), "gemm_residual: resid must be [M, N]");
+  const int64_t N = w_kn ? W.size(1) : W.size(0);
+  const int64_t K = w_kn ? W.size(0) : W.size(1);
+  TORCH_CHECK(A.size(1) == K, "gemm_residual: K mismatch");
+  TORCH_CHECK(resid.size(0) == A.size(0) && resid.size(1) == N, "gemm_residual: resid must be [M, N]");
   const at::cuda::CUDAGuard guard(A.device());
   torch::Tensor out =
-      out_opt.has_value() && out_opt->defined() ? *out_opt : torch::empty({A.size(0), W.size(0)}, A.options());
+      out_opt.has_value() && out_opt->defined() ? *out_opt : torch::empty({A.size(0), N}, A.options());
   check_operand(out, "out");
-  TORCH_CHECK(out.size(0) == A.size(0) && out.size(1) == W.size(0), "gemm_residual: out must be [M, N]");
+  TORCH_CHECK(out.size(0) == A.size(0) && out.size(1) == N, "gemm_residual: out must be [M, N]");
   if (A.size(0) == 0) return out;
-  GemmParams p = make_params(static_cast<int>(A.size(0)), static_cast<int>(W.size(0)), static_cast<int>(A.size(1)), status);
+  GemmParams p = make_params(static_cast<int>(A.size(0)), static_cast<int>(N), static_cast<int>(K), status);
   TORCH_CHECK(p.N % 8 == 0, "gemm_residual: N must be a multiple of 8");
   p.alpha = static_cast<float>(alpha);
   p.sumsq = const_cast<float*>(opt_f32(sumsq, p.M, "sumsq"));
-  Operand oa{&A, false}, ow{&W, false};
-  dispatch_bn<kResidual, false, false>(bn > 0 ? static_cast<int>(bn) : choose_bn(p.N), oa, ow, &out, &resid, p,
-                                       at::cuda::getCurrentCUDAStream());
+  Operand oa{&A, false}, ow{&W, w_kn};
+  const int b = bn > 0 ? static_cast<int>(bn) : choose_bn(p.N);
+  auto s = at::cuda::getCurrentCUDAStream();
+  if (w_kn)
+    dispatch_bn<kResidual, false, true>(b, oa, ow, &out, &resid, p, s);
+  else
+    dispatch_bn<kResidual, false, false>(b, oa, ow, &out, &resid, p, s);
   return out;
 }
 

@@ -1,10 +1,10 @@
 // Allocation-free entry point of the attention backward pass.
 //
 // This entry point has no counterpart in the reference implementation. It exists for
-// callers that cannot allocate device memory: code running inside a CUDA graph being
-// captured by a framework that forbids allocation during capture, engines with a fixed
-// memory pool that reserve all device memory up front, and plain C / FFI hosts that link
-// the library without PyTorch's caching allocator. The regular entry point
+// callers that cannot call cudaMalloc: engines that reserve all device memory in a fixed
+// pool at start-up and forbid any later allocation, and plain C / FFI hosts that link
+// this library without PyTorch's caching allocator (so a per-call scratch buffer has
+// nowhere to come from). The regular entry point
 // (`nori::attn_bwd`, Python `ops.attention_bwd`) allocates a per-call scratch vector for
 // the row dot products dO . O; this variant keeps that scratch in a fixed file-scope
 // device array instead.
@@ -34,10 +34,13 @@ extern "C" {
 //   stream           : the stream to run on (0 = legacy default stream).
 //
 // Returns cudaSuccess, or cudaErrorInvalidValue when BH * Nq exceeds
-// NORI_NOALLOC_MAX_ROWS or an argument is malformed (nori_attention_bwd_noalloc_error()
-// then gives a one-line reason). The first call on each device looks up the scratch
-// array's device address with cudaGetSymbolAddress; make that first call before any
-// stream capture. Every call on a device shares the one scratch array and overwrites
+// NORI_NOALLOC_MAX_ROWS or an argument is malformed: a null or misaligned pointer (the
+// bf16 tensors and dq 16-byte aligned, lse 4-byte aligned), a layout stride that is
+// negative or not a multiple of 8 elements, or a layout d1 / d2 that is not positive
+// (nori_attention_bwd_noalloc_error() then gives a one-line reason). Every check runs
+// before any work is queued, so a rejected call leaves dq, dk, dv and the scratch alone.
+// The first call on each device looks up the scratch array's device address with
+// cudaGetSymbolAddress; make that first call before any stream capture. Every call on a device shares the one scratch array and overwrites
 // it, so calls that may overlap on the GPU (different streams without ordering) race.
 cudaError_t nori_attention_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout,
                                        const float* lse, float* dq, void* dk, void* dv, const int64_t* lq,

@@ -8,6 +8,8 @@ honouring ``SYNTHEFY_NORI_HF_REPO`` / ``SYNTHEFY_NORI_HF_FILENAME`` for the base
 from __future__ import annotations
 
 import os
+from dataclasses import dataclass, field
+from pathlib import Path
 
 DEFAULT_FILENAME = "nori.pt"
 NORI_MODELS = {
@@ -40,6 +42,33 @@ def download_checkpoint(model: str = "nori-6m", filename: str | None = None, cac
             f"could not fetch {repo_for(model)}/{fn} ({type(exc).__name__}: {exc}); pass model_path= to a local "
             "checkpoint or weights='random' for a random-init model"
         ) from exc
+
+
+@dataclass(frozen=True)
+class HubCheckpoint:
+    """A published checkpoint: hub repository + file, an optional environment variable
+    that points at a local copy, and free-form metadata (calibrated thresholds,
+    architecture notes)."""
+
+    repo_id: str
+    filename: str = DEFAULT_FILENAME
+    env_var: str | None = None
+    meta: dict = field(default_factory=dict)
+
+
+def resolve_checkpoint(entry: HubCheckpoint | None, explicit=None) -> Path:
+    """Local checkpoint file, from the first source that names one: the caller's
+    ``explicit`` path, then ``entry.env_var``, then a hub download of ``entry``.  A named
+    local path that does not exist is an error (never silently replaced by a download)."""
+    for candidate in (explicit, os.environ.get(entry.env_var) if entry is not None and entry.env_var else None):
+        if candidate:
+            path = Path(candidate).expanduser()
+            if not path.is_file():
+                raise FileNotFoundError(f"checkpoint file does not exist: {path}")
+            return path
+    if entry is None:
+        raise ValueError("no checkpoint source: pass a file path or a registered model name")
+    return Path(download_checkpoint(entry.repo_id, filename=entry.filename))
 
 
 LIMIX_REPO_ID = "stableai-org/LimiX-2M"

@@ -265,6 +265,10 @@ class FeaturesTransformer(nn.Module):
         from synthefy_nori_b200.ops.fused_layer import bump_weight_generation
 
         bump_weight_generation()
+        ref = getattr(self, "_nori_layout_owner", None)
+        owner = ref() if ref is not None else None
+        if owner is not None:  # a trainer's persistent bf16 layouts: refresh them from the new weights
+            owner.resync_layouts()
         return result
 
     # ------------------------------------------------------------------ dispatch
@@ -282,7 +286,22 @@ class FeaturesTransformer(nn.Module):
                 "synthefy_nori_b200 native extension is not built; run `python setup.py build_ext --inplace` "
                 f"(import error: {ops.native_import_error()})"
             )
-        return self.two_phase_config is None and self.layer_arch == "smf" and self.pre_norm and self.norm_type == "rmsnorm"
+        if self.two_phase_config is not None:
+            return False
+        from synthefy_nori_b200.ops.fused_layer import model_supported
+
+        if not model_supported(self):
+            if self.impl == "native":
+                raise NotImplementedError("impl='native': the native kernels do not cover this layer variant")
+            if not getattr(self, "_nori_warned_variant", False):
+                import warnings
+
+                warnings.warn("the native sm_100a kernels do not cover this encoder-layer variant (log-n or learnable "
+                              "attention temperature, qk-norm, shared K/V heads, a non-SwiGLU MLP, the fmfmsm arch "
+                              "or post-norm); running the PyTorch path", RuntimeWarning, stacklevel=3)
+                self._nori_warned_variant = True
+            return False
+        return True
 
     # ------------------------------------------------------------------ inputs
     def _build_x_preprocess_inputs(self, x: torch.Tensor, eval_pos: int):

@@ -1,8 +1,8 @@
 """Python entry points of the native kernels.
 
 Every function requires CUDA tensors and the built extension; there is no silent
-fallback (``lib()`` raises if ``_C`` is missing).  The fp32 PyTorch references used
-by the numerics tests live in ``synthefy_nori_b200.ops.reference``.
+fallback (``lib()`` raises if ``_C`` is missing).  The numerics tests compare each
+kernel with a plain fp32 PyTorch statement of the same operation, written in the test.
 """
 
 from __future__ import annotations
@@ -76,9 +76,10 @@ def gemm_swiglu(a: torch.Tensor, w_interleaved: torch.Tensor, row_scale=None, bn
     return _lib().gemm_swiglu(a, w_interleaved, row_scale, status_word(a.device), bn)
 
 
-def gemm_residual(a, w, resid, alpha: float, sumsq=None, bn: int = 0, out=None) -> torch.Tensor:
-    """bf16 ``resid + alpha * (a @ w.T)``; adds each new row's sum of squares to ``sumsq``."""
-    return _lib().gemm_residual(a, w, resid, float(alpha), sumsq, status_word(a.device), bn, out)
+def gemm_residual(a, w, resid, alpha: float, sumsq=None, bn: int = 0, out=None, w_kn: bool = False) -> torch.Tensor:
+    """bf16 ``resid + alpha * (a @ W.T)``; adds each new row's sum of squares to ``sumsq``.
+    ``w`` is ``W`` [N, K], or with ``w_kn=True`` the same matrix stored [K, N]."""
+    return _lib().gemm_residual(a, w, resid, float(alpha), sumsq, status_word(a.device), bn, out, bool(w_kn))
 
 
 def gemm_wgrad(dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor, bn: int = 0, splits: int = 0,
@@ -178,9 +179,12 @@ def grad_sumsq(g: torch.Tensor, out: torch.Tensor) -> None:
 
 
 def adamw_ema_step(p, g, m, v, *, lr, beta1, beta2, eps, wd, step, ema=None, p_bf16=None, norm_sq=None,
-                   ema_decay=0.999, max_norm=0.0, grad_scale=1.0) -> None:
+                   ema_decay=0.999, max_norm=0.0, grad_scale=1.0, skip=None) -> None:
+    """Clip + AdamW + EMA in one pass over flat fp32 buffers.  ``skip`` (fp32 device
+    scalar, optional): when > 0 the step leaves everything untouched (a step rejected on
+    the device, with no host synchronisation); a non-finite gradient norm does the same."""
     _lib().adamw_ema(p, g, m, v, ema, p_bf16, norm_sq, float(lr), float(beta1), float(beta2), float(eps), float(wd),
-                     int(step), float(ema_decay), float(max_norm), float(grad_scale))
+                     int(step), float(ema_decay), float(max_norm), float(grad_scale), skip)
 
 
 def quantize_int8(x: torch.Tensor):

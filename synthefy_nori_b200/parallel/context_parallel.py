@@ -1,4 +1,4 @@
-"""Context-row-sharded inference over NVLink peer memory.
+"""Context-row-sharded inference over NVLink peer memory (one long table whose context rows are split over the GPUs).
 
 One table's context rows are split over the ranks of one node. Every rank embeds the
 whole context (the embedding is cheap and the column statistics must be global), then
@@ -159,7 +159,7 @@ class ShardedContextPredictor:
             base = li * self.kv_layer_bytes
             self.cache.view(base + self.kv_off, R * 2 * E, torch.int8).copy_(q8.reshape(-1))
             self.cache.view(base + self.sc_off, R * 2 * H, torch.float32).copy_(sc.reshape(-1))
-            x = ops.gemm_residual(o, wb["wo_self_t"], x, layer.alpha)
+            x = ops.gemm_residual(o, wb["wo_self"], x, layer.alpha, w_kn=True)
             torch.cuda.synchronize(self.device)
             dist.barrier(self.group)  # peers finished reading this layer's staging buffer
             wq = {"wb": wb}
@@ -196,7 +196,7 @@ class ShardedContextPredictor:
             ops.lib().attn_fwd_q8_shards(q, kv_ptrs, sc_ptrs, self.n_rows, [0] * self.world, [0] * self.world, o, None,
                                          list(lq), list(lkv), list(ls), list(lq), E, H, T * H, nq, D,
                                          1.0 / math.sqrt(D))
-            x = ops.gemm_residual(o, wb["wo_cross_t"], x, layer.alpha)
+            x = ops.gemm_residual(o, wb["wo_cross"], x, layer.alpha, w_kn=True)
             wq = {"wb": wb}
             x = _mlp_forward(layer, wq, x)
             x = _feat_forward(layer, wq, x, g)

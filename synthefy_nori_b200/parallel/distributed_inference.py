@@ -3,7 +3,7 @@
 Parity target: reference ``inference/inference_method.py:48-209`` (query rows strided over
 ranks by a non-padding sampler, every rank predicts its rows against the replicated
 context, results gathered and re-ordered; enabled by ``inference_with_DDP=True``) and
-BASELINE config 5 (independent tables data-parallel over GPUs).  The reference gathers
+independent tables spread over the GPUs (table data parallelism).  The reference gathers
 pickled CPU objects (``all_gather_object``); here the per-rank outputs stay on the device
 and are gathered with one collective of a padded tensor (NVLink on a B200 node), then
 un-strided on every rank.

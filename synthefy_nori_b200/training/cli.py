@@ -118,81 +118,86 @@ class Run:
         self.shape_rng = torch.Generator().manual_seed(args.seed + 17)  # shared across ranks
         self.step = 0
 
-    # optimizer state as full vectors (gathered when sharded over ranks)
-    def _opt(self):
+    # ------------------------------------------------------------------ checkpoint state
+    def _flat_layout(self):
         tr = self.trainer
         if tr.peer is not None:
-            return None
-        return tr.opt
+            return tr.peer.params, tr.peer.offsets
+        return tr.flat.params, tr.flat.offsets
+
+    def _per_param(self, full: torch.Tensor) -> dict:
+        """Split a full flat vector into ``{parameter name: tensor}`` (layout-independent,
+        so a checkpoint resumes under any world size or gradient path)."""
+        names = {id(p): n for n, p in self.trainer.model.named_parameters()}
+        params, offsets = self._flat_layout()
+        return {names[id(p)]: full[o : o + p.numel()].view(p.shape).detach().cpu() for p, o in zip(params, offsets)}
+
+    def _to_flat(self, per: dict, like: torch.Tensor) -> torch.Tensor:
+        names = {id(p): n for n, p in self.trainer.model.named_parameters()}
+        params, offsets = self._flat_layout()
+        full = torch.zeros_like(like)
+        for p, o in zip(params, offsets):
+            full[o : o + p.numel()].copy_(per[names[id(p)]].reshape(-1).to(full))
+        return full
 
     def state(self) -> dict:
-        from synthefy_nori_b200.ops.fused_layer import bump_weight_generation
-
         tr = self.trainer
+        extra = {}
         if tr.peer is not None:
-            m = self._gather_shards(tr.peer.m)
-            v = self._gather_shards(tr.peer.v)
+            m = self._per_param(tr.peer.full_from_owned(tr.peer.m))
+            v = self._per_param(tr.peer.full_from_owned(tr.peer.v))
             ema = tr.peer.gather_ema()
             step = tr.peer.step_count
+        elif tr.muon is not None:  # Muon: its own flat layout (same model + config on resume)
+            m, v, ema, step = tr.opt.m.detach().cpu(), tr.opt.v.detach().cpu(), tr.opt.ema, tr.opt.step_count
+            extra["muon_momentum"] = [b.detach().cpu() for _, _, b in tr.muon.groups]
         else:
-            m, v, ema, step = tr.opt.m, tr.opt.v, tr.opt.ema, tr.opt.step_count
-        bump_weight_generation()
+            m, v = self._per_param(tr.opt.m), self._per_param(tr.opt.v)
+            ema, step = tr.opt.ema, tr.opt.step_count
         sd = {k: t.detach().cpu() for k, t in tr.model.state_dict().items()}
         ema_sd = None
         if ema is not None:
-            flat = tr.peer if tr.peer is not None else tr.flat
             ema_sd = dict(sd)
-            names = {p.data_ptr(): n for n, p in tr.model.named_parameters()}
-            for p, o in zip(flat.params, flat.offsets):
-                ema_sd[names[p.data_ptr()]] = ema[o : o + p.numel()].view(p.shape).detach().cpu()
-        extra = {}
-        if tr.muon is not None:
-            extra["muon_momentum"] = [b.detach().cpu() for _, _, b in tr.muon.groups]
+            ema_sd.update(self._per_param(ema))
+        health = tr.poll()
         return {
             "model_config": self.model_config,
             "model_state_dict": sd,
             "ema_state_dict": ema_sd,
-            "optimizer_state": {"m": m.detach().cpu(), "v": v.detach().cpu(),
-                                "ema": ema.detach().cpu() if ema is not None else None, "step": step, **extra},
+            "optimizer_state": {"m": m, "v": v, "step": step, "layout": "per_parameter" if isinstance(m, dict)
+                                else "muon_flat", **extra},
             "step": self.step,
             "training_config": dataclasses.asdict(self.tcfg) | {"argv": vars(self.args)},
             "rng_state": {"shape": self.shape_rng.get_state(), "torch": torch.get_rng_state()},
             "trainer_state": {"loss_ema": None if tr.loss_ema is None else float(tr.loss_ema),
-                              "steps_done": tr.steps_done, "skipped_steps": tr.skipped_steps},
+                              "steps_done": tr.steps_done, "skipped_steps": health["skipped_steps"]},
         }
 
-    def _gather_shards(self, shard: torch.Tensor) -> torch.Tensor:
-        peer = self.trainer.peer
-        b = peer.bounds.tolist()
-        width = max(b[i + 1] - b[i] for i in range(self.world))
-        buf = torch.zeros(width, device=self.device)
-        buf[: peer.s1 - peer.s0] = shard[: peer.s1 - peer.s0]
-        parts = [torch.empty_like(buf) for _ in range(self.world)]
-        dist.all_gather(parts, buf)
-        return torch.cat([parts[i][: b[i + 1] - b[i]] for i in range(self.world)])
-
     def load(self, ckpt: dict) -> None:
-        from synthefy_nori_b200.ops.fused_layer import bump_weight_generation
-
         tr = self.trainer
-        tr.model.load_state_dict(ckpt["model_state_dict"])
+        tr.model.load_state_dict(ckpt["model_state_dict"])  # also refreshes the bf16 layouts
         o = ckpt["optimizer_state"]
+        ema_sd = ckpt.get("ema_state_dict")
         if tr.peer is not None:
-            s0, s1 = tr.peer.s0, tr.peer.s1
-            tr.peer.m[: s1 - s0].copy_(o["m"][s0:s1])
-            tr.peer.v[: s1 - s0].copy_(o["v"][s0:s1])
-            if tr.peer.ema is not None and o["ema"] is not None:
-                tr.peer.ema.copy_(o["ema"][s0:s1])
+            for k in ("m", "v"):
+                getattr(tr.peer, k).copy_(tr.peer.owned_from_full(self._to_flat(o[k], tr.peer.data)))
+            if tr.peer.ema is not None and ema_sd is not None:
+                tr.peer.ema.copy_(tr.peer.owned_from_full(self._to_flat(ema_sd, tr.peer.data)))
             tr.peer.step_count = int(o["step"])
-        else:
+        elif tr.muon is not None:
             tr.opt.m.copy_(o["m"])
             tr.opt.v.copy_(o["v"])
-            if tr.opt.ema is not None and o["ema"] is not None:
-                tr.opt.ema.copy_(o["ema"])
+            if tr.opt.ema is not None and ema_sd is not None:
+                tr.opt.ema.copy_(self._to_flat(ema_sd, tr.flat.data))
             tr.opt.step_count = int(o["step"])
-            if tr.muon is not None:
-                for (_, _, b), src in zip(tr.muon.groups, o["muon_momentum"]):
-                    b.copy_(src)
+            for (_, _, b), src in zip(tr.muon.groups, o["muon_momentum"]):
+                b.copy_(src)
+        else:
+            tr.opt.m.copy_(self._to_flat(o["m"], tr.opt.m))
+            tr.opt.v.copy_(self._to_flat(o["v"], tr.opt.v))
+            if tr.opt.ema is not None and ema_sd is not None:
+                tr.opt.ema.copy_(self._to_flat(ema_sd, tr.flat.data))
+            tr.opt.step_count = int(o["step"])
         self.step = int(ckpt["step"])
         ts = ckpt.get("trainer_state") or {}
         if ts.get("loss_ema") is not None:
@@ -201,7 +206,6 @@ class Run:
         tr.skipped_steps = int(ts.get("skipped_steps", 0))
         self.shape_rng.set_state(ckpt["rng_state"]["shape"])
         torch.set_rng_state(ckpt["rng_state"]["torch"])
-        bump_weight_generation()
 
     def train_one(self) -> float:
         from synthefy_nori_b200.training.prior import sample_shape, scm_prior_batch
@@ -210,10 +214,7 @@ class Run:
         lr = wcd_lr(self.step, a.lr, a.warmup_steps, a.decay_start_step or int(0.8 * a.total_steps), a.total_steps,
                     a.min_lr_ratio)
         tr = self.trainer
-        if tr.peer is not None:
-            tr.peer.lr = lr
-        else:
-            tr.opt.lr = lr
+        tr.set_lr(lr)
         rows, ep = sample_shape(self.prior, self.shape_rng)
         seed = (a.seed * 1_000_003 + self.step * 9973 + self.rank) & 0x7FFFFFFF
         b = scm_prior_batch(self.prior, a.batch_size, rows, ep, seed=seed, device=self.device)
@@ -247,9 +248,12 @@ def main(argv=None) -> int:
     t0, last = time.time(), None
     while run.step < stop:
         last = run.train_one()
-        if rank == 0 and (run.step % args.log_interval == 0 or run.step == stop):
-            print(json.dumps({"step": run.step, "loss": float(last.item()), "elapsed_s": round(time.time() - t0, 1)}),
-                  flush=True)
+        if run.step % args.log_interval == 0 or run.step == stop:
+            run.trainer.raise_if_fatal()  # every rank: the decision is the same everywhere
+            if rank == 0:
+                rec = {"step": run.step, "loss": float(last.item()), "elapsed_s": round(time.time() - t0, 1)}
+                rec.update(run.trainer.poll())
+                print(json.dumps(rec), flush=True)
         if args.checkpoint_dir and (run.step % args.save_interval == 0 or run.step == stop):
             st = run.state()  # collective in the sharded case: every rank takes part
             if rank == 0:

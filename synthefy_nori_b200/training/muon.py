@@ -104,10 +104,14 @@ class HybridMuonAdamW:
         self.groups = [(shape, ps, torch.zeros(len(ps), *shape, device=device)) for shape, ps in groups.items()]
 
     @torch.no_grad()
-    def step(self, grad_scale: float = 1.0) -> None:
+    def step(self, grad_scale: float = 1.0, skip: torch.Tensor | None = None) -> None:
+        """``skip`` (device scalar, > 0 = reject the step): every update below is blended
+        with ``keep = (skip <= 0)`` on the device, so a rejected step changes nothing and
+        no host synchronisation is needed."""
         from synthefy_nori_b200 import ops
 
         self.step_count += 1
+        keep = None if skip is None else (skip.reshape(()) <= 0).float()
         grad = self.flat.grad
         if grad_scale != 1.0:
             grad.mul_(grad_scale)
@@ -124,25 +128,38 @@ class HybridMuonAdamW:
             g = torch.stack([p.grad.reshape(m, n) for p in ps])
             if clip is not None:
                 g.mul_(clip)
-            buf.mul_(self.momentum).add_(g)
+            if keep is None:
+                buf.mul_(self.momentum).add_(g)
+            else:  # buf <- momentum buf + g when kept, unchanged when rejected
+                buf.mul_(1.0 - keep * (1.0 - self.momentum)).add_(g * keep)
             eff = g.add(buf, alpha=self.momentum) if self.nesterov else buf
             upd = newton_schulz(eff, self.ns_steps)
             s = _scale(m, n, self.adjust_lr)
             for i, p in enumerate(ps):
-                if self.wd:
-                    p.mul_(1.0 - lr_m * self.wd)
-                p.add_(upd[i].view_as(p), alpha=-lr_m * s)
+                if keep is None:
+                    if self.wd:
+                        p.mul_(1.0 - lr_m * self.wd)
+                    p.add_(upd[i].view_as(p), alpha=-lr_m * s)
+                else:
+                    if self.wd:
+                        p.mul_(1.0 - lr_m * self.wd * keep)
+                    p.add_(upd[i].view_as(p) * (-lr_m * s * keep))
         if self.split < self.flat.numel:
             data, g = self.flat.data[self.split :], grad[self.split :]
             if data.is_cuda and ops.native_available():
                 ops.adamw_ema_step(data, g, self.m, self.v, lr=self.lr, beta1=self.betas[0], beta2=self.betas[1],
                                    eps=self.eps, wd=self.wd, step=self.step_count, ema=None,
                                    norm_sq=self.norm_sq if clip is not None else None, ema_decay=0.0,
-                                   max_norm=self.max_grad_norm or 0.0, grad_scale=1.0)
+                                   max_norm=self.max_grad_norm or 0.0, grad_scale=1.0,
+                                   skip=None if skip is None else skip.reshape(1).float())
             else:
-                self._adamw_torch(data, g * (clip if clip is not None else 1.0))
+                if keep is not None and float(keep) == 0.0:  # CPU path: a host decision costs nothing
+                    pass
+                else:
+                    self._adamw_torch(data, g * (clip if clip is not None else 1.0))
         if self.ema is not None:
-            self.ema.lerp_(self.flat.data, 1.0 - self.ema_decay)
+            w = 1.0 - self.ema_decay
+            self.ema.lerp_(self.flat.data, w if keep is None else keep * w)
 
     def _adamw_torch(self, p, g):
         b1, b2 = self.betas

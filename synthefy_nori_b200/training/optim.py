@@ -53,9 +53,10 @@ class FusedAdamWEMA:
         self.step_count = 0
         self.norm_sq = torch.zeros(1, device=flat.data.device, dtype=torch.float32)
 
-    def step(self, grad_scale: float = 1.0) -> None:
+    def step(self, grad_scale: float = 1.0, skip: torch.Tensor | None = None) -> None:
         """One AdamW + EMA step on the flat buffers. ``grad_scale`` multiplies the
-        gradients first (e.g. 1 / world_size after a sum-reduction)."""
+        gradients first (e.g. 1 / world_size after a sum-reduction); ``skip`` (device
+        scalar, > 0 = reject the step) is read by the kernel, so no host synchronisation."""
         from synthefy_nori_b200 import ops
 
         self.step_count += 1
@@ -66,7 +67,8 @@ class FusedAdamWEMA:
                            beta2=self.betas[1], eps=self.eps, wd=self.wd, step=self.step_count, ema=self.ema,
                            norm_sq=self.norm_sq if self.max_grad_norm else None,
                            ema_decay=self.ema_decay if self.ema_decay is not None else 0.0,
-                           max_norm=self.max_grad_norm or 0.0, grad_scale=grad_scale)
+                           max_norm=self.max_grad_norm or 0.0, grad_scale=grad_scale,
+                           skip=None if skip is None else skip.reshape(1).float())
 
     def ema_state_dict(self, model) -> dict:
         """Model state dict with EMA weights in place of the trainable parameters."""

@@ -77,3 +77,19 @@ def test_tc_backward_matches_reference(BH, Nq, Nk, D):
     for got, want in ((dq, qf.grad), (dk.float(), kf.grad), (dv.float(), vf.grad)):
         rel = ((got - want).norm() / want.norm()).item()
         assert rel < 2e-2, rel
+
+
+def test_exp2_poly_against_exp2f():
+    """The softmax's FMA-pipe 2^x (minimax cubic + exponent-field add) against CUDA's
+    exp2f over its whole input range [-125, 0]: relative error within the stated 7.5e-5."""
+    from synthefy_nori_b200 import ops
+
+    x = torch.linspace(-125.0, 0.0, 2_000_001, device="cuda")
+    x = torch.cat([x, -torch.rand(1_000_000, device="cuda") * 3.0, torch.tensor([-0.5, -0.25, -1e-7, 0.0],
+                                                                                device="cuda")])
+    got = ops.lib().exp2_poly_eval(x.contiguous())
+    ref = torch.exp2(x)  # CUDA exp2f
+    rel = ((got.double() - ref.double()) / ref.double()).abs()
+    assert float(rel.max()) <= 7.6e-5
+    exact = torch.exp2(x.double())
+    assert float(((got.double() - exact) / exact).abs().max()) <= 7.6e-5

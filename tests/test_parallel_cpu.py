@@ -104,3 +104,95 @@ def test_distributed_inference_on_gloo():
         p.join(timeout=60)
     assert all(p.exitcode == 0 for p in ps)
     assert all(v < 1e-5 for _, _, v in res), res
+
+
+def _leave_worker(rank, world, port, q):
+    import datetime
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
+    from synthefy_nori_b200.parallel.health import RankFailure, RankHealth
+
+    store = dist.distributed_c10d._get_default_store()
+    health = RankHealth(store, rank, world, stale_s=30.0)
+    g = torch.ones(4)
+    health.beat(0)
+    dist.all_reduce(g)  # step 0 on both ranks
+    dist.barrier()
+    if rank == 1:
+        health.leave()  # leaves between steps, with nothing in flight
+        q.put((rank, "left", None))
+        q.close()
+        q.join_thread()  # flush the queue before the hard exit
+        os._exit(0)  # no destroy_process_group: the process just ends
+    import time
+
+    time.sleep(1.0)
+    t0 = time.time()
+    try:
+        health.check(1)
+        q.put((rank, "check", "no error"))
+    except RankFailure as e:
+        q.put((rank, "check", e.ranks))
+    t1 = time.time()
+    try:
+        dist.all_reduce(g)  # the next collective ends with an error, within the group timeout
+        q.put((rank, "collective", "no error"))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, "collective", type(e).__name__))
+    q.put((rank, "times", (t1 - t0, time.time() - t1)))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+@pytest.mark.timeout(120)
+def test_rank_leaving_between_steps_is_detected():
+    import socket
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_leave_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = {}
+    for _ in range(4):
+        r, k, v = q.get(timeout=90)
+        got[(r, k)] = v
+    for p in ps:
+        p.join(timeout=30)
+    assert got[(0, "check")] == [1]  # the host-side check names the rank that left
+    assert got[(0, "collective")] != "no error"
+    t_check, t_coll = got[(0, "times")]
+    assert t_check < 2.0 and t_coll < 30.0
+
+
+def test_rank_health_staleness():
+    from synthefy_nori_b200.parallel.health import RankFailure, RankHealth
+
+    class Store(dict):
+        def set(self, k, v):
+            self[k] = v.encode() if isinstance(v, str) else v
+
+        def get(self, k):
+            return dict.__getitem__(self, k)
+
+        def check(self, keys):
+            return all(k in self for k in keys)
+
+    st = Store()
+    a, b = RankHealth(st, 0, 2, stale_s=60.0, max_lag=2), RankHealth(st, 1, 2, stale_s=60.0, max_lag=2)
+    a.beat(5)
+    b.beat(5)
+    a.check(6)
+    with pytest.raises(RankFailure) as e:
+        a.check(9)  # rank 1 is 4 steps behind
+    assert e.value.ranks == [1]
+    st["nori/health/1"] = b"5 0.0"  # a heartbeat from long ago
+    with pytest.raises(RankFailure):
+        a.check(5)

@@ -1,0 +1,87 @@
+"""Planning of the bf16 weight-layout refresh / all-gather (host side): the segment
+table covers every parameter once, is 4-element aligned, and, executed by a plain
+Python statement of the kernel's index arithmetic, reproduces the layouts the native
+layer would otherwise build by casting; the bucket / piece geometry of the peer step."""
+
+import torch
+
+from synthefy_nori_b200.models.config import preset_config
+from synthefy_nori_b200.ops.weight_layouts import segment_plan
+from synthefy_nori_b200.parallel.peer_reduce import owned_pieces, plan_buckets
+from synthefy_nori_b200.utils.loading import build_model
+
+
+def _flat(model, align=64):
+    params = [p for p in model.parameters() if p.requires_grad]
+    offs, o = {}, 0
+    for p in params:
+        offs[id(p)] = o
+        o += -(-p.numel() // align) * align
+    flat = torch.zeros(o)
+    for p in params:
+        flat[offs[id(p)] : offs[id(p)] + p.numel()] = p.detach().reshape(-1)
+    return params, offs, flat
+
+
+def _emulate(segs, chunks, flat, shapes):
+    out = {li: {k: torch.full(s, float("nan")) for k, s in sh.items()} for li, sh in shapes.items()}
+    for si, j0, j1 in chunks:
+        src, rows, cols, dst, doff, drs = segs[si]
+        assert j0 % 4 == 0 and j1 % 4 == 0 or j1 == rows * cols
+        for j in range(j0, j1, 4):
+            f = src + j
+            vals = flat[f : f + 4]
+            if dst is None:
+                continue
+            r, c = divmod(j, cols)
+            t = out[dst[0]][dst[1]].view(-1)
+            t[doff + r * drs + c : doff + r * drs + c + 4] = vals
+    return out
+
+
+def test_segment_plan_reproduces_cast_layouts():
+    from synthefy_nori_b200.ops.fused_layer import _bf, layer_weights
+
+    torch.manual_seed(0)
+    model = build_model(preset_config("nori-tiny"))
+    params, offs, flat = _flat(model)
+    segs, chunks, shapes = segment_plan(model, offs, with_gather=True)
+    # every trainable parameter is covered exactly once
+    cover = torch.zeros(flat.numel(), dtype=torch.int32)
+    for src, rows, cols, *_ in segs:
+        assert src % 4 == 0 and cols % 4 == 0
+        cover[src : src + rows * cols] += 1
+    for p in params:
+        o = offs[id(p)]
+        assert bool((cover[o : o + p.numel()] == 1).all())
+    got = _emulate(segs, chunks, flat, shapes)
+    for li, layer in enumerate(model.transformer_encoder.layers):
+        w = layer_weights(layer)
+        E = layer.embed_dim
+        want = {"w_ctx": w["w_ctx"], "w_q": w["w_q"], "wo_self": w["wo_self"].reshape(E, E),
+                "wo_cross": w["wo_cross"].reshape(E, E), "w_gu": w["w_gu"], "w_down": w["w_down"],
+                "w_fqkv": w["w_fqkv"], "w_fo": w["w_fo"].reshape(E, E)}
+        for k, t in want.items():
+            torch.testing.assert_close(got[li][k], t.detach().float(), atol=0, rtol=0)
+            assert _bf(t).shape == got[li][k].shape
+
+
+def test_bucket_geometry():
+    sizes = [1000, 64, 5000, 3, 70000, 128]
+    for world in (1, 2, 3, 8):
+        offs, numel, buckets = plan_buckets(sizes, bucket_elems=4096, world=world)
+        assert buckets[0][0] == 0 and buckets[-1][1] == numel
+        for (s, e, piece), nxt in zip(buckets, buckets[1:] + [None]):
+            assert s % 64 == 0 and e % 64 == 0 and piece % 64 == 0 and piece * world >= e - s
+            if nxt is not None:
+                assert nxt[0] == e
+        # the owned pieces of all ranks tile every bucket exactly
+        cover = torch.zeros(numel, dtype=torch.int32)
+        total = 0
+        for r in range(world):
+            tab, n = owned_pieces(buckets, world, r)
+            total += n
+            for roff, f, length in tab:
+                assert f % 64 == 0 and length % 64 == 0
+                cover[f : f + length] += 1
+        assert total == numel and bool((cover == 1).all())

@@ -1,8 +1,9 @@
 """The allocation-free attention-backward entry point, called through its exported C
 symbol, against the regular (allocating) entry point.
 
-Callers that cannot allocate device memory (allocation-free graph capture, fixed
-memory pools, plain C hosts) use ``nori_attention_bwd_noalloc``; it must produce the
+Callers that cannot call cudaMalloc (engines that reserve all device memory in a fixed
+pool at start-up, plain C / FFI hosts without PyTorch's allocator) use
+``nori_attention_bwd_noalloc``; it must produce the
 same gradients as ``ops.attention_bwd`` on consecutive calls, since every call reuses the
 same fixed scratch array. This file is collected last on purpose.
 """
@@ -81,3 +82,40 @@ def test_noalloc_rejects_oversized_problem():
     rc = fn(*([z.data_ptr()] * 9), lay, lay, lay, lay, lay, lay, lay, 2048, 1024, 64, 64, 0.125, 0)
     assert rc != 0
     assert b"NORI_NOALLOC_MAX_ROWS" in err()
+
+
+def _valid_args(n=16):
+    z = torch.zeros(4096, device="cuda")
+    lay = (0, 0, 0, 64, 1, 1)
+    return z, lay
+
+
+def test_noalloc_rejects_misaligned_pointer_without_side_effects():
+    fn, err = _lib()
+    z, lay = _valid_args()
+    dq = torch.full((64,), 3.0, device="cuda")
+    ptrs = [z.data_ptr()] * 9
+    ptrs[0] = z.data_ptr() + 2  # q misaligned
+    ptrs[6] = dq.data_ptr()
+    a = _arr(lay)
+    rc = fn(*ptrs, a, a, a, a, a, a, a, 1, 1, 1, 64, 0.125, 0)
+    torch.cuda.synchronize()
+    assert rc != 0 and b"aligned" in err()
+    assert bool((dq == 3.0).all())  # nothing was queued: dq not cleared
+
+
+def test_noalloc_rejects_zero_layout_divisor():
+    fn, err = _lib()
+    z, _ = _valid_args()
+    dq = torch.full((64,), 3.0, device="cuda")
+    ptrs = [z.data_ptr()] * 9
+    ptrs[6] = dq.data_ptr()
+    good, bad = _arr((0, 0, 0, 64, 1, 1)), _arr((0, 0, 0, 64, 1, 0))  # d2 = 0
+    rc = fn(*ptrs, good, bad, good, good, good, good, good, 1, 1, 1, 64, 0.125, 0)
+    torch.cuda.synchronize()
+    assert rc != 0 and b"d1 and d2" in err()
+    assert bool((dq == 3.0).all())
+    # a stride that is not a multiple of 8 elements is rejected too
+    odd = _arr((0, 0, 0, 60, 1, 1))
+    rc = fn(*ptrs, odd, good, good, good, good, good, good, 1, 1, 1, 64, 0.125, 0)
+    assert rc != 0 and b"multiples of 8" in err()
