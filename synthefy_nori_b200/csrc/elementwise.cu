@@ -216,16 +216,19 @@ torch::Tensor sumsq_to_scale(const torch::Tensor& ssq, int64_t E, double eps) {
 // quantiles [K] ascending, inv_var [B] = 1 / clamp(var_b, 0.01).
 // Writes grad [R, K] (same dtype as pred) of the batch-mean objective and adds the
 // objective into loss[0]. One CTA of 256 threads per row.
+// ldp / ldg: row strides of pred and grad; grad columns [K, kpad) are written as zeros
+// (a padded gradient feeds a GEMM whose N was rounded up to a multiple of 8).
 template <typename T>
 __global__ void pinball_kernel(const T* __restrict__ pred, const float* __restrict__ target,
                                const float* __restrict__ quantiles, const float* __restrict__ inv_var, int64_t R,
                                int K, int nq, int B, float tail_w, float mono_w, float mse_w, T* __restrict__ grad,
-                               float* __restrict__ loss) {
+                               float* __restrict__ loss, int64_t ldp, int64_t ldg, int kpad) {
   const int64_t r = blockIdx.x;
   if (r >= R) return;
   const int b = static_cast<int>(r / nq);
-  const T* p = pred + r * K;
-  T* g = grad + r * K;
+  const T* p = pred + r * ldp;
+  T* g = grad + r * ldg;
+  for (int k = K + threadIdx.x; k < kpad; k += blockDim.x) g[k] = static_cast<T>(0.f);
   const float t = target[r];
   const float iv = inv_var[b];
   __shared__ float red[3][8];
@@ -318,17 +321,46 @@ std::vector<torch::Tensor> pinball_fused(const torch::Tensor& pred, const torch:
         reinterpret_cast<const __nv_bfloat16*>(pred.data_ptr()), target.data_ptr<float>(),
         quantiles.data_ptr<float>(), inv_var.data_ptr<float>(), R, K, static_cast<int>(nq), B,
         static_cast<float>(tail_w), static_cast<float>(mono_w), static_cast<float>(mse_w),
-        reinterpret_cast<__nv_bfloat16*>(grad.data_ptr()), loss.data_ptr<float>());
+        reinterpret_cast<__nv_bfloat16*>(grad.data_ptr()), loss.data_ptr<float>(), K, K, K);
   } else {
     TORCH_CHECK(pred.scalar_type() == at::kFloat, "pinball: bf16 or fp32 pred");
     pinball_kernel<float><<<R, 256, 0, s>>>(pred.data_ptr<float>(), target.data_ptr<float>(),
                                             quantiles.data_ptr<float>(), inv_var.data_ptr<float>(), R, K,
                                             static_cast<int>(nq), B, static_cast<float>(tail_w),
                                             static_cast<float>(mono_w), static_cast<float>(mse_w),
-                                            grad.data_ptr<float>(), loss.data_ptr<float>());
+                                            grad.data_ptr<float>(), loss.data_ptr<float>(), K, K, K);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {loss, grad};
+}
+
+// Strided bf16 variant for the native head: pred [R, >= K] (row stride pred.stride(0)),
+// grad written into a preallocated bf16 [R, kpad] (columns >= K zeroed); returns the loss.
+torch::Tensor pinball_fused_into(const torch::Tensor& pred, int64_t K, const torch::Tensor& target,
+                                 const torch::Tensor& quantiles, const torch::Tensor& inv_var, int64_t nq,
+                                 double tail_w, double mono_w, double mse_w, torch::Tensor& grad) {
+  TORCH_CHECK(pred.is_cuda() && pred.scalar_type() == at::kBFloat16 && pred.dim() == 2 && pred.stride(1) == 1 &&
+                  pred.size(1) >= K,
+              "pinball_into: bf16 [R, >= K] pred with unit column stride");
+  TORCH_CHECK(grad.scalar_type() == at::kBFloat16 && grad.is_contiguous() && grad.dim() == 2 &&
+                  grad.size(0) == pred.size(0) && grad.size(1) >= K,
+              "pinball_into: contiguous bf16 grad [R, kpad >= K]");
+  TORCH_CHECK(target.scalar_type() == at::kFloat && target.is_contiguous() && target.numel() == pred.size(0),
+              "pinball_into: fp32 target [R]");
+  TORCH_CHECK(quantiles.scalar_type() == at::kFloat && quantiles.numel() == K, "pinball_into: fp32 quantiles [K]");
+  TORCH_CHECK(nq > 0 && pred.size(0) % nq == 0 && inv_var.numel() == pred.size(0) / nq, "pinball_into: R = B * nq");
+  const at::cuda::CUDAGuard guard(pred.device());
+  auto loss = torch::zeros({1}, pred.options().dtype(at::kFloat));
+  const int64_t R = pred.size(0);
+  if (R == 0) return loss;
+  pinball_kernel<__nv_bfloat16><<<R, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(pred.data_ptr()), target.data_ptr<float>(), quantiles.data_ptr<float>(),
+      inv_var.data_ptr<float>(), R, static_cast<int>(K), static_cast<int>(nq), static_cast<int>(R / nq),
+      static_cast<float>(tail_w), static_cast<float>(mono_w), static_cast<float>(mse_w),
+      reinterpret_cast<__nv_bfloat16*>(grad.data_ptr()), loss.data_ptr<float>(), pred.stride(0), grad.stride(0),
+      static_cast<int>(grad.size(1)));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return loss;
 }
 
 // ------------------------------------------------------------------ optimizer

@@ -1,0 +1,101 @@
+"""The native input side (column statistics, scientific-RBF features with the
+precomposed fusion GEMM, LayerNorm kernels, target-aware gate + y token + token-row
+layout) against the fp32 PyTorch modules: forward token rows and every parameter
+gradient; the fp64 scientific decomposition at powers of ten."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _tables(B, S, F, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(B, S, F, device="cuda", generator=g)
+    x[:, :, 1] *= 1e4  # large magnitudes
+    x[:, :, 2] = x[:, :, 2] * 1e-6  # small magnitudes
+    x[:, :, 3] = 0.0  # a constant (invalid) column
+    x[:, :, 4] = torch.floor(x[:, :, 4] * 3)  # integer codes
+    x[torch.rand(B, S, F, device="cuda", generator=g) < 0.1] = float("nan")
+    x[0, 3, 5] = float("inf")
+    y = torch.randn(B, S, device="cuda", generator=g)
+    return x, y
+
+
+def _reference_rows(model, x, y_ctx, ep):
+    xe, ye, pre, pad, _ = model.embed(x, y_ctx, ep, "reg")
+    tokens = torch.cat((xe.float(), ye.unsqueeze(2).float()), 2)
+    B, S, T, E = tokens.shape
+    return torch.cat((tokens[:, :ep].reshape(-1, E), tokens[:, ep:].reshape(-1, E)), 0), pre
+
+
+@pytest.mark.parametrize("preset", ["nori-tiny", "nori-6m"])
+def test_native_embed_matches_torch(preset):
+    from synthefy_nori_b200.models.config import preset_config
+    from synthefy_nori_b200.ops.embed import embed_supported, native_embed
+    from synthefy_nori_b200.utils.loading import build_model
+
+    torch.manual_seed(0)
+    model = build_model(preset_config(preset)).cuda().train()
+    assert embed_supported(model)
+    with torch.no_grad():  # a non-trivial target-aware gate
+        if model.column_y_aware_alpha is not None:
+            model.column_y_aware_alpha.fill_(0.3)
+        model.reg_target_aware_embedding.weight.normal_(0, 0.5)
+    B, S, F, ep = 3, 70, 12, 50
+    x, y = _tables(B, S, F)
+    params = [p for p in model.parameters() if p.requires_grad]
+    X, pre, pad, T = native_embed(model, x, y[:, :ep], ep)
+    ref, pre_ref = _reference_rows(model, x, y[:, :ep], ep)
+    assert X.shape == ref.shape and T == F // model.features_per_group + 1
+    scale = float(ref.abs().max())
+    err = (X.float() - ref).abs()
+    assert float(err.max()) <= 3e-2 * scale, float(err.max())
+    torch.testing.assert_close(pre["_valid_feature_num"], pre_ref["_valid_feature_num"].float())
+    dX = torch.randn_like(ref)
+    g_nat = torch.autograd.grad(X.float(), params, dX, allow_unused=True)
+    g_ref = torch.autograd.grad(ref, params, dX, allow_unused=True)
+    names = [n for n, p in model.named_parameters() if p.requires_grad]
+    checked = 0
+    for n, a, b in zip(names, g_nat, g_ref):
+        if b is None:
+            continue
+        assert a is not None, n
+        sc = float(b.abs().max()) + 1e-6
+        assert float((a.float() - b).abs().max()) <= 6e-2 * sc, (n, float((a.float() - b).abs().max()), sc)
+        checked += 1
+    assert checked >= 10
+
+
+def test_rbf_decomposition_at_powers_of_ten():
+    """Cells exactly at / next to powers of ten: the fp64 decomposition picks the same
+    exponent as the reference's fp64 path, so the features agree."""
+    from synthefy_nori_b200 import ops
+    from synthefy_nori_b200.models.config import preset_config
+    from synthefy_nori_b200.utils.loading import build_model
+
+    model = build_model(preset_config("nori-tiny")).cuda()
+    rbf = model.encoder_x[0].numeric_mlp
+    vals = []
+    for e in range(-9, 10):
+        for f in (1.0, 0.99999994, 1.0000001, 9.999999, 5.0):
+            v = f * 10.0 ** e
+            vals += [v, -v]
+    vals += [0.0, 1e-12, -3e11]
+    v = torch.tensor(vals, device="cuda", dtype=torch.float32)
+    n = v.numel()
+    fpg = 2
+    n = n - n % fpg
+    x = v[:n].view(1, n // fpg, fpg).contiguous()  # one table, each row a token of fpg cells
+    Fd = fpg
+    mean = torch.zeros(1, Fd, device="cuda")
+    std = torch.ones(1, Fd, device="cuda")
+    gscale = torch.ones(1, 1, device="cuda")
+    g, b = rbf.control_table()
+    table = torch.cat([g, b], -1).float().contiguous()
+    out = ops.lib().rbf_aug_fwd(x, mean, std, gscale, table, rbf.norm.weight.detach(), rbf.norm.bias.detach(),
+                                rbf.centers.float().contiguous(), float(rbf.sigma), float(rbf.norm.eps), fpg, 136)
+    # values clip at +-100 after standardisation, exactly as the model does
+    ref = rbf.rbf_features(x.clamp(-100, 100).reshape(-1)).float()
+    got = out.view(-1, 136)[:, : fpg * 66].reshape(-1, fpg, 66)[:, :, :64].reshape(-1, 64).float()
+    torch.testing.assert_close(got, ref, atol=3e-2, rtol=2e-2)

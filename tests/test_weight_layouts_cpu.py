@@ -64,6 +64,12 @@ def test_segment_plan_reproduces_cast_layouts():
         for k, t in want.items():
             torch.testing.assert_close(got[li][k], t.detach().float(), atol=0, rtol=0)
             assert _bf(t).shape == got[li][k].shape
+    if "head" in shapes:
+        l1, l2 = model.reg_y_decoder[0], model.reg_y_decoder[3]
+        torch.testing.assert_close(got["head"]["w1"], l1.weight.detach(), atol=0, rtol=0)
+        K = l2.out_features
+        torch.testing.assert_close(got["head"]["w2"][:K], l2.weight.detach(), atol=0, rtol=0)
+        assert bool(torch.isnan(got["head"]["w2"][K:]).all())  # pad rows: never written (allocated as zeros)
 
 
 def test_bucket_geometry():
