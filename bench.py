@@ -141,16 +141,29 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- shapes
 def step_shapes(args, n: int):
-    """(rows, eval_pos) of every step: rows ~ U[min_rows, max_rows], context fraction
-    ~ U[0.5, 0.9]; with a palette, its P draws are cycled."""
+    """(rows, eval_pos) of every step.  rows ~ U[min_rows, max_rows], context fraction
+    ~ U[0.5, 0.9].  With a palette of P shapes, the P shapes are the distribution's
+    stratum midpoints (rows and fractions at quantiles (i + 1/2) / P, fractions paired with
+    rows by a seeded permutation), so the palette has the distribution's mean and mean
+    square row count (attention cost grows with rows^2); the steps cycle through it."""
     g = torch.Generator().manual_seed(args.seed)
-    draws = []
-    for _ in range(args.shape_palette if args.shape_palette > 0 else n):
+    if args.shape_palette > 0:
+        P = args.shape_palette
+        perm = torch.randperm(P, generator=g).tolist()
+        draws = []
+        for i in range(P):
+            rows = int(round(args.min_rows + (i + 0.5) * (args.max_rows - args.min_rows) / P))
+            frac = 0.5 + 0.4 * (perm[i] + 0.5) / P
+            draws.append((rows, min(max(1, int(rows * frac)), rows - 1)))
+        order = torch.randperm(P, generator=g).tolist()
+        draws = [draws[i] for i in order]
+        return [draws[i % P] for i in range(n)]
+    out = []
+    for _ in range(n):
         rows = int(torch.randint(args.min_rows, args.max_rows + 1, (1,), generator=g).item())
         frac = 0.5 + 0.4 * float(torch.rand(1, generator=g).item())
-        ep = min(max(1, int(rows * frac)), rows - 1)
-        draws.append((rows, ep))
-    return [draws[i % len(draws)] for i in range(n)]
+        out.append((rows, min(max(1, int(rows * frac)), rows - 1)))
+    return out
 
 
 def prior_cfg(args):
@@ -659,8 +672,8 @@ def main():
                 "loss": "pinball 999 + 0.05 monotonicity",
                 "optimizer": "AdamW + EMA 0.999, clip 1.0",
                 "l2": "per-step working set is several GB (> 126 MB L2); no flush needed",
-                "shapes": (f"palette of {args.shape_palette} (rows, ctx) draws cycled" if args.shape_palette > 0
-                           else "fresh draw per step"),
+                "shapes": (f"stratified palette of {args.shape_palette} (rows, ctx) shapes cycled"
+                           if args.shape_palette > 0 else "fresh draw per step"),
             },
             "grad_reduction": reduction,
             "clocks": clk,

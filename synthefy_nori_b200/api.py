@@ -146,13 +146,34 @@ class NoriRegressor(RegressorMixin, BaseEstimator):
 
         if getattr(self, "predictor_", None) is None:
             model = self._load_model()
-            dtype = self._resolve_memory(model)
+            if getattr(self, "memory_policy_", None) is None or self.memory_policy_.rung is None:
+                self._resolve_memory(model)
             pol = self.memory_policy_
+            dtype, placement, block_rows = pol.placement()
             self.predictor_ = NoriPredictor(model, self.device_, inference_config=self.inference_config,
                                             n_estimators=self.n_estimators, cache_dtype=dtype,
                                             query_chunk_size=self.query_chunk_size, seed=self.random_state,
-                                            reuse_context_cache=pol.reuse_context_cache)
+                                            reuse_context_cache=pol.reuse_context_cache, placement=placement,
+                                            stream_block_rows=block_rows)
         return self.predictor_
+
+    def _escalate_memory(self, exc) -> bool:
+        """After an out-of-memory error: move the policy to its next rung (warning) and
+        drop the predictor so the next attempt rebuilds the cache there."""
+        from synthefy_nori_b200.inference.degradation import MemoryEscalatedWarning
+
+        pol = getattr(self, "memory_policy_", None)
+        nxt = pol.next_rung() if pol is not None else None
+        if nxt is None:
+            return False
+        warnings.warn(f"out of GPU memory on the {pol.rung} cache rung; retrying on {nxt}", MemoryEscalatedWarning,
+                      stacklevel=4)
+        self.memory_policy_ = pol.escalated(nxt)
+        self.predictor_ = None
+        self.context_ = self.context_yj_ = None
+        if torch.cuda.is_available():
+            torch.cuda.empty_cache()
+        return True
 
     def _resolve_memory(self, model) -> str:
         """Pick the cache rung for this table (reference ``MemoryPolicy.resolve``)."""
@@ -179,7 +200,7 @@ class NoriRegressor(RegressorMixin, BaseEstimator):
             keep = np.sort(rng.choice(self.X_train_.shape[0], self.X_train_.shape[0] - pol.dropped_context_rows,
                                       replace=False))
             self.X_train_, self.y_train_ = self.X_train_[keep], self.y_train_[keep]
-        dtype = "int8" if pol.rung in ("resident_int8", "context_sharded_int8") or pol.cache_dtype == "int8" else "bf16"
+        dtype = pol.placement()[0]
         if dtype == "int8" and pol.cache_dtype == "bf16":
             warnings.warn("context cache stored int8 to fit the memory budget", CacheQuantizedWarning, stacklevel=3)
         return dtype
@@ -291,7 +312,12 @@ class NoriRegressor(RegressorMixin, BaseEstimator):
         return getattr(self, attr)
 
     def _raw(self, X: np.ndarray) -> torch.Tensor:
-        return self._get_predictor().predict_raw(self._context(), X)
+        while True:  # out of memory: escalate down the rung ladder and retry
+            try:
+                return self._get_predictor().predict_raw(self._context(), X)
+            except torch.cuda.OutOfMemoryError as exc:
+                if not self._escalate_memory(exc):
+                    raise
 
     def _distribution(self, X: np.ndarray) -> dict:
         pred = self._get_predictor()

@@ -23,6 +23,11 @@ class CacheQuantizedWarning(DegradedPipelineWarning):
     """The context cache was stored int8 although bf16 was requested."""
 
 
+class MemoryEscalatedWarning(DegradedPipelineWarning):
+    """An out-of-memory error moved the context cache to a lower rung (int8, host offload,
+    streamed blocks) and the prediction was retried there."""
+
+
 @contextlib.contextmanager
 def strict_pipeline(*categories: type[Warning]):
     """Raise instead of warn for the given degradation categories (default: all)."""

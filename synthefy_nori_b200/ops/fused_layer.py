@@ -569,6 +569,106 @@ class NativeKV:
         return (self.kv.view(-1, 2, g.H, g.D).float() * self.scale.view(-1, 2, g.H, 1)).to(BF16).view(-1, 2 * g.E)
 
 
+class HostKV:
+    """A layer's cross-attention K/V kept in pinned host memory, in row blocks.
+
+    Host-offload rung: one block per layer; the query pass copies the whole layer to the
+    device just before it runs (the next layer's copy overlaps this layer's compute), so
+    the device holds two layers' K/V instead of all of them.  Streamed rung: blocks of
+    ``block_rows`` context rows per table; the query pass attends to one block at a time
+    (double-buffered copies) and merges the partial results by their log-sum-exps, so the
+    device never holds a full layer.  Reference: ``model/kv_cache_scaling.py``
+    (``ScalableSeqKV`` offload, ``BlockwiseSeqKV`` streaming)."""
+
+    def __init__(self, blocks: list, g: Geometry, quantized: bool):
+        self.blocks = blocks  # [(n_rows, kv_host [B * n_rows * T, 2E], scale_host | None)]
+        self.g = g
+        self.quantized = quantized
+        self.n_rows = g.ep
+
+    @classmethod
+    def from_native(cls, kv: NativeKV, block_rows: int | None) -> "HostKV":
+        g = kv.g
+        n = g.ep
+        step = n if not block_rows or block_rows >= n else int(block_rows)
+        blocks = []
+        kv4 = kv.kv.view(g.B, n, g.T, -1)
+        sc4 = kv.scale.view(g.B, n, g.T, -1) if kv.scale is not None else None
+        for r0 in range(0, n, step):
+            r1 = min(n, r0 + step)
+            kb = kv4[:, r0:r1].reshape(-1, kv4.shape[-1]).to("cpu").pin_memory()
+            sb = sc4[:, r0:r1].reshape(-1, sc4.shape[-1]).to("cpu").pin_memory() if sc4 is not None else None
+            blocks.append((r1 - r0, kb, sb))
+        return cls(blocks, g, kv.scale is not None)
+
+    def nbytes(self) -> int:
+        return sum(k.numel() * k.element_size() + (s.numel() * 4 if s is not None else 0) for _, k, s in self.blocks)
+
+
+class _Stager:
+    """Double-buffered host -> device copies of K/V blocks on a side stream."""
+
+    def __init__(self, device):
+        self.device = device
+        self.stream = torch.cuda.Stream(device)
+        self.bufs = [None, None]
+        self.events = [None, None]
+        self.slot = 0
+
+    def _ensure(self, i, shape_kv, dtype, shape_sc):
+        b = self.bufs[i]
+        need_kv = int(torch.Size(shape_kv).numel())
+        need_sc = int(torch.Size(shape_sc).numel()) if shape_sc is not None else 0
+        if b is None or b[0].numel() < need_kv or (need_sc and (b[1] is None or b[1].numel() < need_sc)) \
+                or b[0].dtype != dtype:
+            kvb = torch.empty(need_kv, device=self.device, dtype=dtype)
+            scb = torch.empty(need_sc, device=self.device, dtype=torch.float32) if need_sc else None
+            self.bufs[i] = (kvb, scb)
+        return self.bufs[i]
+
+    def issue(self, block):
+        """Start copying ``block`` into the next buffer; returns a handle for ``wait``."""
+        n, kh, sh = block
+        i = self.slot
+        self.slot ^= 1
+        kvb, scb = self._ensure(i, kh.shape, kh.dtype, sh.shape if sh is not None else None)
+        cur = torch.cuda.current_stream(self.device)
+        self.stream.wait_stream(cur)  # the buffer's previous user is done
+        with torch.cuda.stream(self.stream):
+            kd = kvb[: kh.numel()].view(kh.shape)
+            kd.copy_(kh, non_blocking=True)
+            sd = None
+            if sh is not None:
+                sd = scb[: sh.numel()].view(sh.shape)
+                sd.copy_(sh, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+        return (n, kd, sd, ev)
+
+    @staticmethod
+    def wait(handle):
+        n, kd, sd, ev = handle
+        torch.cuda.current_stream(kd.device).wait_event(ev)
+        return n, kd, sd
+
+
+def place_caches(caches: list, placement: str, block_rows: int | None = None) -> list:
+    """Move built caches to pinned host memory: ``"offload"`` (one block per layer) or
+    ``"stream"`` (blocks of ``block_rows`` context rows)."""
+    if placement == "resident":
+        return caches
+    if placement not in ("offload", "stream"):
+        raise ValueError(f"unknown cache placement {placement!r}")
+    rows = None if placement == "offload" else (block_rows or 4096)
+    out = []
+    for c in caches:
+        kv = c["seq_kv"]
+        out.append({"seq_kv": HostKV.from_native(kv, rows)})
+        del kv
+    torch.cuda.empty_cache()
+    return out
+
+
 # bf16 scratch for the dequantised K/V of one layer, shared by all layers of a query pass
 _DEQUANT_SCRATCH: dict = {}
 DEQUANT_SCRATCH_MAX_FRACTION = 0.25
@@ -766,17 +866,59 @@ def run_stack_cached(model, tokens: torch.Tensor, caches: list) -> torch.Tensor:
         raise ValueError(f"expected {len(model.transformer_encoder.layers)} layer caches, got {len(caches)}")
     B, nq, T, E = tokens.shape
     x = tokens.to(BF16).reshape(-1, E).contiguous()
-    for layer, c in zip(model.transformer_encoder.layers, caches):
-        kv: NativeKV = c["seq_kv"]
+    layers = list(model.transformer_encoder.layers)
+    host = isinstance(caches[0]["seq_kv"], HostKV) if caches else False
+    stager = _Stager(x.device) if host else None
+    pending = None
+    if host and len(caches[0]["seq_kv"].blocks) == 1:  # offload: prefetch layer 0 now
+        pending = stager.issue(caches[0]["seq_kv"].blocks[0])
+    for li, (layer, c) in enumerate(zip(layers, caches)):
+        kv = c["seq_kv"]
         g = Geometry(B=B, ep=kv.g.ep, nq=nq, T=T, E=E, H=model.nhead)
         if kv.g.B != B:
             raise ValueError(f"cache was built for {kv.g.B} tables, queries have {B}")
         w = layer_weights(layer)
         w["wb"] = _cached_bf16(layer, w)
-        x = _seq_query_forward(layer, w, x, kv, g)
+        if isinstance(kv, HostKV) and len(kv.blocks) == 1:
+            n, kd, sd = _Stager.wait(pending)
+            if li + 1 < len(caches):  # the next layer's copy overlaps this layer
+                pending = stager.issue(caches[li + 1]["seq_kv"].blocks[0])
+            x = _seq_query_forward(layer, w, x, NativeKV(kd, kv.g, sd), g)
+        elif isinstance(kv, HostKV):
+            x = _seq_query_forward_streamed(layer, w, x, kv, g, stager)
+        else:
+            x = _seq_query_forward(layer, w, x, kv, g)
         x = _mlp_forward(layer, w, x)
         x = _feat_forward(layer, w, x, g)
     return x.view(B, nq, T, E).to(tokens.dtype)
+
+
+@torch.no_grad()
+def _seq_query_forward_streamed(layer, w, x, hkv: HostKV, g: Geometry, stager: "_Stager"):
+    """Query attention against a context streamed in row blocks from host memory: each
+    block's partial output and log-sum-exp are merged online (``attn_lse_merge``)."""
+    E, D = g.E, g.D
+    rs = ops.rms_scale(x, layer.layer_norm_eps)
+    yq = ops.gemm(x, w["wb"]["w_q"], row_scale=rs)
+    q = _qass_apply(w["qp"][8:], w["qmode"], yq, g.ep, g.H, D) if w["qmode"] else yq
+    lq = _seq_layout(g.nq, g, E)
+    BTH = g.B * g.T * g.H
+    acc = torch.empty(x.shape[0], E, device=x.device, dtype=torch.float32)
+    lse_acc = torch.empty(BTH, g.nq, device=x.device, dtype=torch.float32)
+    o = torch.empty(x.shape[0], E, device=x.device, dtype=BF16)
+    lse = torch.empty(BTH, g.nq, device=x.device, dtype=torch.float32)
+    blocks = hkv.blocks
+    nxt = stager.issue(blocks[0])
+    for bi in range(len(blocks)):
+        n, kd, sd = _Stager.wait(nxt)
+        if bi + 1 < len(blocks):
+            nxt = stager.issue(blocks[bi + 1])
+        gb = Geometry(B=g.B, ep=n, nq=g.nq, T=g.T, E=E, H=g.H)
+        kvb = NativeKV(kd, gb, sd).dequantize() if sd is not None else kd
+        l2 = _seq_layout(n, gb, 2 * E)
+        _attn(q, kvb[:, :E], kvb[:, E:], o, lq, l2, lq, BTH, g.nq, n, D, lse=lse)
+        ops.lib().attn_lse_merge(acc, lse_acc, o, lse, g.T, g.H, g.nq, bi == 0)
+    return ops.gemm_residual(acc.to(BF16), w["wb"]["wo_cross"], x, _layer_alpha(layer), w_kn=True)
 
 
 @torch.no_grad()

@@ -136,6 +136,16 @@ def load_model(model_path, mask_prediction: bool = False, base_config_path=None,
     return model
 
 
+def load_state_into(model, path, base_config_path=None) -> None:
+    """Copy a checkpoint's weights (EMA weights when present) into an existing model of
+    the same architecture; strict, so a mismatched architecture fails loudly."""
+    ckpt = safe_torch_load(path)
+    _config, weights = _extract(ckpt, path, base_config_path)
+    if any(k.startswith("_orig_mod.") for k in weights):
+        weights = {k.removeprefix("_orig_mod."): v for k, v in weights.items()}
+    model.load_state_dict(weights)
+
+
 def save_release_checkpoint(model: FeaturesTransformer, config: dict, path, inference_config: dict | None = None) -> None:
     """Write the slim release format ``{"model_config", "model_state_dict"[, "inference_config"]}``."""
     payload: dict[str, Any] = {"model_config": dict(config), "model_state_dict": model.state_dict()}

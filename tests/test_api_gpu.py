@@ -77,3 +77,25 @@ def test_cuda_graph_replay_matches_eager():
     torch.testing.assert_close(b, a, atol=2e-3, rtol=2e-3)
     b2 = graphed.predict_raw(cg, X[600:700])  # replay
     torch.testing.assert_close(b2, a[:100], atol=2e-3, rtol=2e-3)
+
+
+@pytest.mark.parametrize("placement,rows", [("offload", None), ("stream", 64), ("stream", 37)])
+@pytest.mark.parametrize("dtype", ["bf16", "int8"])
+def test_host_offloaded_and_streamed_caches_match_resident(placement, rows, dtype):
+    """Host-offloaded caches (a layer copied in just before it runs) and streamed caches
+    (row blocks merged by their log-sum-exps) give the resident cache's predictions."""
+    from synthefy_nori_b200.models.config import preset_config
+    from synthefy_nori_b200.utils.loading import build_model
+
+    torch.manual_seed(0)
+    dev = torch.device("cuda")
+    model = build_model(preset_config("nori-tiny")).to(dev).eval()
+    x = torch.randn(2, 300, 6, device=dev)
+    y = x[..., 0] - 0.5 * x[..., 1] ** 2
+    with torch.no_grad():
+        ref = model.apply_context_cache(x[:, 200:], model.build_context_cache(x[:, :200], y[:, :200],
+                                                                              cache_dtype=dtype)).float()
+        c = model.build_context_cache(x[:, :200], y[:, :200], cache_dtype=dtype, placement=placement,
+                                      stream_block_rows=rows)
+        got = model.apply_context_cache(x[:, 200:], c).float()
+    torch.testing.assert_close(got, ref, atol=3e-2, rtol=3e-2)

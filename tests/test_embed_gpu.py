@@ -61,8 +61,9 @@ def test_native_embed_matches_torch(preset):
         if b is None:
             continue
         assert a is not None, n
-        sc = float(b.abs().max()) + 1e-6
-        assert float((a.float() - b).abs().max()) <= 6e-2 * sc, (n, float((a.float() - b).abs().max()), sc)
+        # bf16 activations and gradients against an fp32 oracle: relative L2 error per tensor
+        rel = float((a.float() - b).norm() / (b.norm() + 1e-12))
+        assert rel <= 3e-2, (n, rel)
         checked += 1
     assert checked >= 10
 

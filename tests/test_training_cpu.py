@@ -104,3 +104,45 @@ def test_masks():
     assert torch.isnan(xm[:, 10:]).sum() == bm.sum() and not torch.isnan(xm[:, :10]).any()
     with pytest.raises(ValueError):
         create_masks(4, 4, 0.2, "diag")
+
+
+def test_shape_sampler_budget_buckets_and_palette():
+    from synthefy_nori_b200.training.shapes import FEATURE_BUCKETS, SAMPLE_BUCKETS, ShapeConfig, ShapeSampler
+
+    cfg = ShapeConfig(min_samples=256, max_samples=8192, min_features=4, max_features=512, features_per_group=2,
+                      max_budget=500_000, dim_bias_samples=2.2, dim_bias_features=1.5, bucketed=True)
+    s = ShapeSampler(cfg, 0)
+    seen = [s.sample() for _ in range(400)]
+    for n, f, r in seen:
+        assert n in SAMPLE_BUCKETS and f in FEATURE_BUCKETS and n * f <= 500_000 and f % 2 == 0
+        assert r in (0.3, 0.4, 0.5, 0.6, 0.7, 0.8)
+    # the same seed gives the same stream (shared across ranks); biasing pushes draws up
+    s2 = ShapeSampler(cfg, 0)
+    assert [s2.sample() for _ in range(400)] == seen
+    plain = ShapeSampler(ShapeConfig(min_samples=256, max_samples=8192, bucketed=False), 1)
+    biased = ShapeSampler(ShapeConfig(min_samples=256, max_samples=8192, bucketed=False, dim_bias_samples=3.0), 1)
+    assert sum(biased.sample()[0] for _ in range(300)) > sum(plain.sample()[0] for _ in range(300))
+    pal = ShapeSampler(ShapeConfig(shape_palette=[(512, 10, 1.0), (1024, 20, 3.0)], context_ratio_palette=[0.7]), 2)
+    draws = [pal.sample() for _ in range(200)]
+    assert {(n, f) for n, f, _ in draws} == {(512, 10), (1024, 20)} and {r for *_, r in draws} == {0.7}
+
+
+def test_icl_health_mask():
+    from synthefy_nori_b200.training.icl_filter import health_mask
+
+    X = torch.randn(4, 50, 3)
+    y = torch.randn(4, 50)
+    y[1, 10] = float("nan")  # non-finite target
+    y[2, :30] = 1.0  # constant context target
+    X[3, :30] = 0.0  # no varying context feature
+    assert health_mask(X, y, 30).tolist() == [True, False, False, False]
+
+
+def test_curriculum_tier_args():
+    from synthefy_nori_b200.training.cli import parse_args
+    from synthefy_nori_b200.training.curriculum import TIERS, tier_args
+
+    for t in TIERS:
+        a = parse_args(tier_args(t) + ["--checkpoint-dir", "/tmp/x"])
+        assert a.max_budget == TIERS[t]["budget"] and a.gradient_accumulation == TIERS[t]["accum"]
+        assert a.prior == "mixture" and a.optimizer == "muon"
