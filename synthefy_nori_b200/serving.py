@@ -21,35 +21,20 @@ import argparse
 import threading
 
 import numpy as np
-from pydantic import BaseModel, ConfigDict
+
+from synthefy_nori_b200.client.data_models import MemoryReport, NoriPredictRequest
 
 _LOCK = threading.Lock()
-
-
-class PredictRequest(BaseModel):
-    model_config = ConfigDict(extra="forbid")
-    X_train: list[list[float | None]]
-    y_train: list[float] | list[list[float]]
-    X_test: list[list[float | None]]
-    task: str = "regression"
-    model: str | None = None
-    output_type: str | None = None
-    quantiles: list[float] | None = None
-    discretize: str | None = None
-    categorical_levels: list[float] | None = None
-    memory_policy: str | dict | None = None
-    large_context_policy: str | list[str] | None = None
-    large_context_threshold: int | None = None
-    large_context_seed: int | None = None
-    multi_target_prediction_strategy: str | None = None
-    multi_target_prediction_policy: dict | None = None
+PredictRequest = NoriPredictRequest  # the request body model (validated on arrival)
 
 
 def _matrix(rows) -> np.ndarray:
     return np.array([[np.nan if v is None else float(v) for v in r] for r in rows], dtype=np.float32)
 
 
-def create_app(*, default_model: str = "nori-6m", weights: str | None = None, device=None, api_key: str | None = None):
+def create_app(*, default_model: str = "nori-6m", weights: str | None = None, device=None, api_key: str | None = None,
+               model_paths: dict | None = None):
+    """``model_paths`` maps extra model names (fine-tuned checkpoints) to local files."""
     from fastapi import FastAPI, Header, HTTPException
 
     from synthefy_nori_b200.api import NoriRegressor
@@ -70,7 +55,9 @@ def create_app(*, default_model: str = "nori-6m", weights: str | None = None, de
         name = req.model or default_model
         Xtr, Xte = _matrix(req.X_train), _matrix(req.X_test)
         y = np.asarray(req.y_train, np.float64)
-        kw = dict(model=name, weights=weights, device=device, memory_policy=req.memory_policy,
+        paths = model_paths or {}
+        kw = dict(model=name if name not in paths else None, model_path=paths.get(name),
+                  weights=None if name in paths else weights, device=device, memory_policy=req.memory_policy,
                   large_context_policy=req.large_context_policy, large_context_threshold=req.large_context_threshold,
                   random_state=req.large_context_seed or 0)
         if req.multi_target_prediction_strategy:
@@ -97,7 +84,9 @@ def create_app(*, default_model: str = "nori-6m", weights: str | None = None, de
                     med = reg.predict(Xte, output_type="median")
                     return {"task": req.task, "predictions": med.tolist(), "quantiles": q.tolist()}
                 out = reg.predict(Xte, output_type=ot)
-                return {"task": req.task, "predictions": np.asarray(out, float).tolist()}
+                rep = MemoryReport.from_policy(getattr(reg, "memory_policy_", None)).model_dump()
+                return {"task": req.task, "predictions": np.asarray(out, float).tolist(), "model": name,
+                        "output_type": ot, "memory_report": rep}
         except (ValueError, NotImplementedError) as exc:
             raise HTTPException(status_code=422, detail=str(exc)) from exc
 

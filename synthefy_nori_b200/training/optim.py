@@ -12,6 +12,7 @@ Semantics match ``torch.optim.AdamW`` (decoupled weight decay, bias correction) 
 
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 
@@ -60,6 +61,9 @@ class FusedAdamWEMA:
         from synthefy_nori_b200 import ops
 
         self.step_count += 1
+        if not self.flat.data.is_cuda:
+            self._step_torch(grad_scale, skip)
+            return
         if self.max_grad_norm and self.max_grad_norm > 0:
             self.norm_sq.zero_()
             ops.grad_sumsq(self.flat.grad, self.norm_sq)
@@ -69,6 +73,27 @@ class FusedAdamWEMA:
                            ema_decay=self.ema_decay if self.ema_decay is not None else 0.0,
                            max_norm=self.max_grad_norm or 0.0, grad_scale=grad_scale,
                            skip=None if skip is None else skip.reshape(1).float())
+
+    @torch.no_grad()
+    def _step_torch(self, grad_scale, skip) -> None:
+        """The same update as plain tensor ops (CPU training, e.g. tests and small fine-tunes)."""
+        if skip is not None and float(skip) > 0:
+            return
+        g = self.flat.grad * grad_scale
+        if self.max_grad_norm and self.max_grad_norm > 0:
+            norm = float(g.double().norm())
+            if not np.isfinite(norm):
+                return
+            g = g * min(1.0, self.max_grad_norm / (norm + 1e-6))
+        b1, b2 = self.betas
+        p = self.flat.data
+        p.mul_(1.0 - self.lr * self.wd)
+        self.m.mul_(b1).add_(g, alpha=1 - b1)
+        self.v.mul_(b2).addcmul_(g, g, value=1 - b2)
+        denom = (self.v / (1 - b2 ** self.step_count)).sqrt_().add_(self.eps)
+        p.addcdiv_(self.m, denom, value=-self.lr / (1 - b1 ** self.step_count))
+        if self.ema is not None:
+            self.ema.mul_(self.ema_decay).add_(p, alpha=1 - self.ema_decay)
 
     def ema_state_dict(self, model) -> dict:
         """Model state dict with EMA weights in place of the trainable parameters."""

@@ -60,7 +60,7 @@ def forward_native(model, x: torch.Tensor, y_ctx: torch.Tensor, eval_pos: int, c
     strided view) instead of the head output."""
     from synthefy_nori_b200.ops.fused_layer import Geometry, model_supported, run_stack_tokens, tokens_to_rows
 
-    if not model_supported(model):
+    if not model_supported(model) or not x.is_cuda:
         return _forward_torch(model, x, y_ctx, eval_pos, checkpoint_layers, with_features)
     from synthefy_nori_b200.ops.embed import embed_supported, native_embed
 
@@ -95,7 +95,7 @@ def _forward_torch(model, x, y_ctx, eval_pos, checkpoint_layers, with_features):
     prev = getattr(enc, "gradient_checkpointing", False)
     enc.gradient_checkpointing = checkpoint_layers
     try:
-        with torch.autocast("cuda", dtype=torch.bfloat16):
+        with torch.autocast(x.device.type, dtype=torch.bfloat16, enabled=x.is_cuda):
             xe, ye, pre, pad, _my = model.embed(x, y_ctx, eval_pos, "reg")
             tokens = torch.cat((xe, ye.unsqueeze(2).to(xe.dtype)), 2)
             out = enc(tokens, feature_atten_mask=None, eval_pos=eval_pos)[0]
@@ -298,7 +298,7 @@ class NoriTrainer:
             pred, feat, pre, pad = forward_native(self.model, x_in, y[:, :eval_pos], eval_pos,
                                                   self.cfg.checkpoint_layers, with_features=True)
             feat_loss = masked_feature_loss(feat, x[:, eval_pos:], masks, pre, pad, self.model.features_per_group)
-        elif self.cfg.loss == "pinball" and self.native_head:
+        elif self.cfg.loss == "pinball" and self.native_head and x.is_cuda:
             # native head + pinball objective in one autograd node (no logits kept)
             from synthefy_nori_b200.ops.head import head_pinball_loss
 

@@ -66,13 +66,20 @@ def test_head_pinball_matches_torch(preset):
     loss = head_pinball_loss(model, last, target, q, 0.0, 0.05, 0.0)
     params = [p for p in list(model.encoder_out_norm.parameters()) + list(model.reg_y_decoder.parameters())]
     grads = torch.autograd.grad(loss, [X] + params)
-    # fp32 oracle on the same (bf16-valued) inputs
-    Xr = X.detach().float().requires_grad_(True)
-    pred = model.reg_y_decoder(model.encoder_out_norm(Xr[:, -1])).view(B, nq, -1)
-    ref = pinball_objective_torch(pred, target, q, 0.0, 0.05, 0.0)
-    rgrads = torch.autograd.grad(ref, [Xr] + params)
+    # fp32 oracle on the same (bf16-valued) inputs, and the same module under bf16
+    # autocast (the precision the PyTorch path trains at): the native node must be within
+    # twice the autocast path's own error of the fp32 oracle (relative L2 per tensor)
+    def torch_grads(autocast):
+        Xr = X.detach().float().requires_grad_(True)
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
+            pred = model.reg_y_decoder(model.encoder_out_norm(Xr[:, -1])).view(B, nq, -1)
+        ref = pinball_objective_torch(pred.float(), target, q, 0.0, 0.05, 0.0)
+        return ref, torch.autograd.grad(ref, [Xr] + params)
+
+    ref, rgrads = torch_grads(False)
+    _, agrads = torch_grads(True)
     torch.testing.assert_close(loss.float(), ref.float(), atol=2e-3, rtol=1e-2)
-    for gn, gr in zip(grads, rgrads):
-        scale = float(gr.abs().max()) + 1e-12
-        assert float((gn.float() - gr).abs().max()) <= 4e-2 * scale, (gn.shape, float((gn.float() - gr).abs().max()),
-                                                                     scale)
+    for gn, gr, ga in zip(grads, rgrads, agrads):
+        err = float((gn.float() - gr).norm() / (gr.norm() + 1e-30))
+        base = float((ga.float() - gr).norm() / (gr.norm() + 1e-30))
+        assert err <= max(2 * base, 1e-2), (gn.shape, err, base)
