@@ -243,6 +243,18 @@ def run_ours(args, device, world, rank):
     info = {}
     if trainer.peer is not None:
         info["grad_buckets"] = trainer.peer.describe()
+        # one more (untimed) step with per-bucket CUDA events: when each bucket's reduction
+        # finished relative to the end of the backward pass
+        trainer.peer.record_timeline = True
+        one(args.warmup + args.steps)
+        torch.cuda.synchronize(device)
+        rep = trainer.peer.overlap_report()
+        trainer.peer.record_timeline = False
+        if rep is not None:
+            t = torch.tensor([rep["tail_ms"]], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            rep["tail_ms_max_over_ranks"] = round(float(t.item()), 3)
+            info["grad_overlap"] = rep
     return ms, clk, launches, e2e, float(losses[-1].item()), info
 
 

@@ -107,7 +107,7 @@ class EvalAnalyzer:
         others = [c for c in t.columns if c != focus]
         if focus not in t or not others:
             return pd.DataFrame()
-        best = t[others].max(1) if higher_is_better(metric) else t[others].min(1)
+        best = t[others].max(axis=1) if higher_is_better(metric) else t[others].min(axis=1)
         who = t[others].idxmax(1) if higher_is_better(metric) else t[others].idxmin(1)
         out = pd.DataFrame({focus: t[focus], "best_other": best, "best_other_model": who})
         out["delta"] = (out[focus] - out["best_other"]) * (1 if higher_is_better(metric) else -1)
