@@ -108,7 +108,7 @@ class EvalAnalyzer:
         if focus not in t or not others:
             return pd.DataFrame()
         best = t[others].max(axis=1) if higher_is_better(metric) else t[others].min(axis=1)
-        who = t[others].idxmax(1) if higher_is_better(metric) else t[others].idxmin(1)
+        who = t[others].idxmax(axis=1) if higher_is_better(metric) else t[others].idxmin(axis=1)
         out = pd.DataFrame({focus: t[focus], "best_other": best, "best_other_model": who})
         out["delta"] = (out[focus] - out["best_other"]) * (1 if higher_is_better(metric) else -1)
         return out.sort_values("delta")

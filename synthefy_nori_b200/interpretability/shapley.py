@@ -13,7 +13,19 @@ build computes the indices itself:
 - ``SII`` (order 2, exact, ``d <= 14``): the pairwise Shapley interaction index
   ``sum_S |S|!(d-|S|-2)!/(d-1)! [f(S+ij) - f(S+i) - f(S+j) + f(S)]``.
 
-All coalition rows of one explanation go to the model as one query batch.
+Imputers (what a feature outside the coalition takes):
+
+- ``baseline``: the background mean (most common value for categorical features); one
+  model row per coalition;
+- ``marginal``: ``n_samples`` background rows drawn once per explainer; the coalition's
+  value is the mean prediction over them (interventional Shapley values);
+- ``conditional``: per coalition, the ``n_samples`` background rows nearest to ``x`` in
+  the coalition's own features (standardised Euclidean distance) supply the absent
+  features, a nearest-neighbour estimate of the conditional distribution (the reference's
+  ``shapiq`` conditional imputer fits a generative model for the same purpose).
+
+All coalition rows of one explanation (coalitions x samples) go to the model as one query
+batch.
 """
 
 from __future__ import annotations
@@ -33,10 +45,13 @@ class InteractionValues(dict):
 
 class ImputationExplainer:
     def __init__(self, predict_fn, background: np.ndarray, *, categorical_features=(), index: str = "SV",
-                 max_order: int = 1, random_state: int | None = 0):
+                 max_order: int = 1, random_state: int | None = 0, imputer: str = "baseline", n_samples: int = 16):
         if index not in ("SV", "SII", "k-SII"):
             raise ValueError("index must be 'SV', 'SII' or 'k-SII'")
+        if imputer not in ("baseline", "marginal", "conditional"):
+            raise ValueError("imputer must be 'baseline', 'marginal' or 'conditional'")
         self.predict_fn = predict_fn
+        self.imputer = imputer
         bg = np.asarray(background, np.float64)
         base = np.nanmean(bg, 0)
         for c in categorical_features:
@@ -47,10 +62,31 @@ class ImputationExplainer:
         self.index = "SV" if (index == "k-SII" and max_order == 1) else index
         self.max_order = 2 if self.index in ("SII", "k-SII") else 1
         self.rng = np.random.default_rng(random_state)
+        fill = np.where(np.isfinite(bg), bg, self.baseline[None, :])
+        if imputer == "marginal":
+            take = self.rng.choice(len(fill), size=min(n_samples, len(fill)), replace=False)
+            self.samples = fill[take]
+        else:
+            self.samples = fill
+        self.n_samples = min(int(n_samples), len(fill))
+        sd = fill.std(0)
+        self._inv_sd = np.where(sd > 0, 1.0 / np.where(sd > 0, sd, 1.0), 0.0)
 
     def _eval(self, x: np.ndarray, masks: np.ndarray) -> np.ndarray:
-        rows = np.where(masks, x[None, :], self.baseline[None, :]).astype(np.float32)
-        return np.asarray(self.predict_fn(rows), np.float64).reshape(-1)
+        if self.imputer == "baseline":
+            rows = np.where(masks, x[None, :], self.baseline[None, :]).astype(np.float32)
+            return np.asarray(self.predict_fn(rows), np.float64).reshape(-1)
+        S = self.n_samples
+        if self.imputer == "marginal":
+            donors = np.broadcast_to(self.samples[None], (len(masks), S, x.size))
+        else:  # nearest background rows in the coalition's standardised features
+            diff = ((self.samples - x[None, :]) * self._inv_sd[None, :]) ** 2  # [n_bg, d]
+            dist = masks.astype(np.float64) @ diff.T  # [n_masks, n_bg]
+            near = np.argpartition(dist, S - 1, axis=1)[:, :S] if S < dist.shape[1] else \
+                np.broadcast_to(np.arange(dist.shape[1]), dist.shape)
+            donors = self.samples[near]  # [n_masks, S, d]
+        rows = np.where(masks[:, None, :], x[None, None, :], donors).reshape(-1, x.size).astype(np.float32)
+        return np.asarray(self.predict_fn(rows), np.float64).reshape(len(masks), S).mean(1)
 
     def explain(self, x, budget: int = 2048) -> InteractionValues:
         x = np.asarray(x, np.float64).reshape(-1)
@@ -122,10 +158,10 @@ class ImputationExplainer:
 
 
 def get_nori_imputation_explainer(model, data, *, index: str = "k-SII", max_order: int = 2, imputer: str = "baseline",
-                                  random_state: int | None = 0) -> ImputationExplainer:
-    """Explainer over a fitted ``NoriRegressor`` with ``data`` as the background."""
-    if imputer != "baseline":
-        raise NotImplementedError("only the baseline imputer is provided (one model row per coalition)")
+                                  random_state: int | None = 0, n_samples: int = 16) -> ImputationExplainer:
+    """Explainer over a fitted ``NoriRegressor`` with ``data`` as the background;
+    ``imputer`` is ``"baseline"`` (one row per coalition, the fastest), ``"marginal"`` or
+    ``"conditional"`` (``n_samples`` rows per coalition)."""
     cats = list(getattr(model, "categorical_features_", []) or [])
     return ImputationExplainer(lambda rows: model.predict(rows), data, categorical_features=cats, index=index,
-                               max_order=max_order, random_state=random_state)
+                               max_order=max_order, random_state=random_state, imputer=imputer, n_samples=n_samples)
