@@ -2,7 +2,8 @@
 
 The native layer (and the native regression head) reads its weights as bf16 GEMM
 operands in fused layouts: the
-context-row projection ``[Wqkv_self; Wkv_cross]`` (5E rows), the query projection,
+context-row projection ``[Wqkv_self; Wkv_cross]`` (5 x H x Dp rows, Dp = the head width
+rounded up to 8 with zero rows), the query projection,
 the two sequence output projections and the feature output projection in their stored
 ``[E_in, E_out]`` form (read MN-major by the GEMM), the SwiGLU gate/up rows
 interleaved, the down projection and the feature QKV projection.
@@ -29,31 +30,52 @@ CHUNK = 16384  # elements per work item of the sync kernel (a multiple of 4)
 
 
 def _layer_blocks(layer):
-    """(parameter, element offset in it, rows, cols, layout key, dst element offset, dst row stride)."""
+    """(parameter, element offset in it, rows, cols, layout key, dst element offset, dst row
+    stride).  Head-major weights (``[k, H, D, E]`` projections, ``[H, D, E]`` output
+    projections) are written with each head's D rows at a pitch of Dp rows (D rounded up
+    to 8): one block per (k, head) when D is not a multiple of 8, so the padded rows stay
+    zero."""
     E = layer.embed_dim
     sa_self, sa_cross = layer.sequence_attentions[0], layer.sequence_attentions[1]
     mlp = layer.mlp[0]
     fa = layer.feature_attentions[0]
     hd = mlp.w_gate.weight.shape[0]
-    return [
-        (sa_self.qkv_proj_weight, 0, 3 * E, E, "w_ctx", 0, E),
-        (sa_cross.qkv_proj_weight, E * E, 2 * E, E, "w_ctx", 3 * E * E, E),
-        (sa_cross.qkv_proj_weight, 0, E, E, "w_q", 0, E),
-        (sa_self.out_proj_weight, 0, E, E, "wo_self", 0, E),
-        (sa_cross.out_proj_weight, 0, E, E, "wo_cross", 0, E),
-        (mlp.w_gate.weight, 0, hd, E, "w_gu", 0, 2 * E),
-        (mlp.w_up.weight, 0, hd, E, "w_gu", E, 2 * E),
-        (mlp.w_down.weight, 0, E, hd, "w_down", 0, hd),
-        (fa.qkv_proj_weight, 0, 3 * E, E, "w_fqkv", 0, E),
-        (fa.out_proj_weight, 0, E, E, "w_fo", 0, E),
-    ]
+    H = sa_self.num_heads
+    D = E // H
+    Dp = -(-D // 8) * 8
+    A = H * Dp
+
+    def heads(p, k0, nk, key, dst_row0):
+        """``nk`` head-major slabs of ``p`` starting at slab ``k0`` -> layout rows from
+        ``dst_row0`` at the padded pitch."""
+        if Dp == D:
+            return [(p, k0 * H * D * E, nk * H * D, E, key, dst_row0 * E, E)]
+        return [(p, ((k0 + k) * H + h) * D * E, D, E, key, (dst_row0 + k * A + h * Dp) * E, E)
+                for k in range(nk) for h in range(H)]
+
+    return (
+        heads(sa_self.qkv_proj_weight, 0, 3, "w_ctx", 0)
+        + heads(sa_cross.qkv_proj_weight, 1, 2, "w_ctx", 3 * A)
+        + heads(sa_cross.qkv_proj_weight, 0, 1, "w_q", 0)
+        + heads(sa_self.out_proj_weight, 0, 1, "wo_self", 0)
+        + heads(sa_cross.out_proj_weight, 0, 1, "wo_cross", 0)
+        + [
+            (mlp.w_gate.weight, 0, hd, E, "w_gu", 0, 2 * E),
+            (mlp.w_up.weight, 0, hd, E, "w_gu", E, 2 * E),
+            (mlp.w_down.weight, 0, E, hd, "w_down", 0, hd),
+        ]
+        + heads(fa.qkv_proj_weight, 0, 3, "w_fqkv", 0)
+        + heads(fa.out_proj_weight, 0, 1, "w_fo", 0)
+    )
 
 
 def layout_shapes(layer) -> dict:
     E = layer.embed_dim
+    H = layer.sequence_attentions[0].num_heads
+    A = H * (-(-(E // H) // 8) * 8)
     hd = layer.mlp[0].w_gate.weight.shape[0]
-    return {"w_ctx": (5 * E, E), "w_q": (E, E), "wo_self": (E, E), "wo_cross": (E, E), "w_gu": (2 * hd, E),
-            "w_down": (E, hd), "w_fqkv": (3 * E, E), "w_fo": (E, E)}
+    return {"w_ctx": (5 * A, E), "w_q": (A, E), "wo_self": (A, E), "wo_cross": (A, E), "w_gu": (2 * hd, E),
+            "w_down": (E, hd), "w_fqkv": (3 * A, E), "w_fo": (A, E)}
 
 
 def segment_plan(model, offsets: dict, with_gather: bool):

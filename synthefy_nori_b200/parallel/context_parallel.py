@@ -108,6 +108,8 @@ class ShardedContextPredictor:
         self.layers = list(model.transformer_encoder.layers)
         self.E, self.H = model.embed_dim, model.nhead
         self.D = self.E // self.H
+        self.Dp = -(-self.D // 8) * 8  # head width inside the attention buffers (zero padded)
+        self.A = self.H * self.Dp
         self.regions: list[PeerRegion] = []
 
     # ------------------------------------------------------------------ build
@@ -117,7 +119,7 @@ class ShardedContextPredictor:
         if x_ctx.shape[0] != 1:
             raise ValueError("the sharded context path takes one table")
         self.close()  # a rebuild releases the previous table's regions (every rank rebuilds together)
-        model, E, H, D = self.model, self.E, self.H, self.D
+        model, E, H, D, A = self.model, self.E, self.H, self.D, self.A
         tokens, meta = model.context_tokens(x_ctx, y_ctx)
         N, T = tokens.shape[1], tokens.shape[2]
         b = shard_bounds(N, self.world, align=1)
@@ -130,8 +132,8 @@ class ShardedContextPredictor:
         L = len(self.layers)
         # IPC regions: per-layer projection staging (K/V self read by peers) and the cache shard
         max_rows = max(self.n_rows) * T
-        self.stage = PeerRegion(max_rows * 5 * E * 2, self.device, self.group)
-        kv_bytes = _align16(R * 2 * E)
+        self.stage = PeerRegion(max_rows * 5 * A * 2, self.device, self.group)
+        kv_bytes = _align16(R * 2 * A)
         sc_bytes = _align16(R * 2 * H * 4)
         self.kv_layer_bytes = kv_bytes + sc_bytes
         self.cache = PeerRegion(L * self.kv_layer_bytes, self.device, self.group)
@@ -141,7 +143,7 @@ class ShardedContextPredictor:
         self.peer_kv_layer_bytes = []
         for p in range(self.world):
             rp = self.n_rows[p] * T
-            self.peer_kv_layer_bytes.append((_align16(rp * 2 * E), _align16(rp * 2 * E) + _align16(rp * 2 * H * 4)))
+            self.peer_kv_layer_bytes.append((_align16(rp * 2 * A), _align16(rp * 2 * A) + _align16(rp * 2 * H * 4)))
         # device-side flags: slots [0, W) "layer staged", [W, 2W) "layer consumed"
         self.flags = PeerRegion(2 * self.world * 8, self.device, self.group)
         self.flags.view(0, 2 * self.world, torch.int64).zero_()
@@ -149,7 +151,7 @@ class ShardedContextPredictor:
         torch.cuda.synchronize(self.device)
         dist.barrier(self.group)  # flags zeroed everywhere before any rank signals
         W, me = self.world, self.rank
-        blk = [torch.empty(max_rows, 2 * E, device=self.device, dtype=BF16) for _ in range(2)]
+        blk = [torch.empty(max_rows, 2 * A, device=self.device, dtype=BF16) for _ in range(2)]
         copy_stream = torch.cuda.Stream(self.device)
         st = ops.status_word(self.device)
         g_loc = Geometry(B=1, ep=n_loc, nq=0, T=T, E=E, H=H)
@@ -160,15 +162,15 @@ class ShardedContextPredictor:
             rs = ops.rms_scale(x, layer.layer_norm_eps)
             if li > 0:  # every peer copied the previous layer out of my staging buffer
                 ops.lib().peer_wait(self.flags.ptrs[me], W, W, step - 1, self.wait_limit_s, st)
-            y = self.stage.view(0, R * 5 * E, BF16).view(R, 5 * E)
+            y = self.stage.view(0, R * 5 * A, BF16).view(R, 5 * A)
             ops.gemm(x, wb["w_ctx"], row_scale=rs, out=y)
             ops.lib().peer_signal(self.flags.ptrs, me, 0, step)
-            q = _qass_apply(w["qp"][:8], w["qmode"], y[:, :E], N, H, D) if w["qmode"] else y[:, :E].contiguous()
+            q = _qass_apply(w["qp"][:8], w["qmode"], y[:, :A], N, H, D, self.Dp) if w["qmode"] else y[:, :A].contiguous()
             ops.lib().peer_wait(self.flags.ptrs[me], 0, W, step, self.wait_limit_s, st)
-            lq = _seq_layout(n_loc, g_loc, E)
-            acc = torch.empty(R, E, device=self.device, dtype=torch.float32)
+            lq = _seq_layout(n_loc, g_loc, A)
+            acc = torch.empty(R, A, device=self.device, dtype=torch.float32)
             lse_acc = torch.empty(T * H, n_loc, device=self.device, dtype=torch.float32)
-            o = torch.empty(R, E, device=self.device, dtype=BF16)
+            o = torch.empty(R, A, device=self.device, dtype=BF16)
             lse = torch.empty(T * H, n_loc, device=self.device, dtype=torch.float32)
             order = [(me + i) % W for i in range(W)]  # start with the local shard
             cur = torch.cuda.current_stream(self.device)
@@ -179,7 +181,7 @@ class ShardedContextPredictor:
                 rp = self.n_rows[p] * T
                 copy_stream.wait_stream(cur)  # the buffer's previous reader is done
                 with torch.cuda.stream(copy_stream):
-                    ops.lib().copy_rows(self.stage.ptrs[p] + E * 2, 5 * E * 2, blk[i % 2], 2 * E * 2, rp, 2 * E * 2)
+                    ops.lib().copy_rows(self.stage.ptrs[p] + A * 2, 5 * A * 2, blk[i % 2], 2 * A * 2, rp, 2 * A * 2)
                     ev = torch.cuda.Event()
                     ev.record(copy_stream)
                 events[i % 2] = ev
@@ -192,17 +194,17 @@ class ShardedContextPredictor:
                 p = order[i]
                 np_ = self.n_rows[p]
                 gp = Geometry(B=1, ep=np_, nq=0, T=T, E=E, H=H)
-                lkv = _seq_layout(np_, gp, 2 * E)
+                lkv = _seq_layout(np_, gp, 2 * A)
                 kvb = blk[i % 2]
-                ops.attention_fwd_tc(q, kvb[:, :E], kvb[:, E:], o, lq=lq, lk=lkv, lv=lkv, lo=lq, BH=T * H, Nq=n_loc,
-                                     Nk=np_, d=D, scale=1.0 / math.sqrt(D), lse=lse)
+                ops.attention_fwd_tc(q, kvb[:, :A], kvb[:, A:], o, lq=lq, lk=lkv, lv=lkv, lo=lq, BH=T * H, Nq=n_loc,
+                                     Nk=np_, d=self.Dp, scale=1.0 / math.sqrt(D), lse=lse)
                 ops.lib().attn_lse_merge(acc, lse_acc, o, lse, T, H, n_loc, i == 0)
             cur.wait_stream(copy_stream)
             ops.lib().peer_signal(self.flags.ptrs, me, W, step)  # done reading every peer's staging
             # int8 cross K/V shard of this layer
-            q8, sc = ops.quantize_int8(y[:, 3 * E :].reshape(R, 2, H, D))
+            q8, sc = ops.quantize_int8(y[:, 3 * A :].reshape(R, 2, H, self.Dp))
             base = li * self.kv_layer_bytes
-            self.cache.view(base + self.kv_off, R * 2 * E, torch.int8).copy_(q8.reshape(-1))
+            self.cache.view(base + self.kv_off, R * 2 * A, torch.int8).copy_(q8.reshape(-1))
             self.cache.view(base + self.sc_off, R * 2 * H, torch.float32).copy_(sc.reshape(-1))
             x = ops.gemm_residual(acc.to(BF16), wb["wo_self"], x, layer.alpha, w_kn=True)
             wq = {"wb": wb}
@@ -218,21 +220,21 @@ class ShardedContextPredictor:
     @torch.no_grad()
     def predict_raw(self, x_q: torch.Tensor) -> torch.Tensor:
         """Quantile outputs ``[1, Nq, K]`` for this rank's query rows ``x_q [1, Nq, F]``."""
-        model, E, H, D, T = self.model, self.E, self.H, self.D, self.T
+        model, E, H, D, T, A, Dp = self.model, self.E, self.H, self.D, self.T, self.A, self.Dp
         tok = model.query_tokens(x_q, self.meta)
         nq = tok.shape[1]
         x = tok.to(BF16).reshape(-1, E).contiguous()
         g = Geometry(B=1, ep=self.N, nq=nq, T=T, E=E, H=H)
-        lq = _seq_layout(nq, g, E)
-        lkv = (0, 2 * E, D, T * 2 * E, T, H)
+        lq = _seq_layout(nq, g, A)
+        lkv = (0, 2 * A, Dp, T * 2 * A, T, H)
         ls = (0, 2 * H, 1, T * 2 * H, T, H)
         for li, layer in enumerate(self.layers):
             w = layer_weights(layer)
             wb = _cached_bf16(layer, w)
             rs = ops.rms_scale(x, layer.layer_norm_eps)
             yq = ops.gemm(x, wb["w_q"], row_scale=rs)
-            q = _qass_apply(w["qp"][8:], w["qmode"], yq, self.N, H, D) if w["qmode"] else yq
-            o = torch.empty(x.shape[0], E, device=self.device, dtype=BF16)
+            q = _qass_apply(w["qp"][8:], w["qmode"], yq, self.N, H, D, Dp) if w["qmode"] else yq
+            o = torch.empty(x.shape[0], A, device=self.device, dtype=BF16)
             kv_ptrs, sc_ptrs = [], []
             for p in range(self.world):
                 kvb, _ = self.peer_kv_layer_bytes[p]
@@ -240,7 +242,7 @@ class ShardedContextPredictor:
                 kv_ptrs.append(self.cache.ptrs[p] + li * layer_bytes)
                 sc_ptrs.append(self.cache.ptrs[p] + li * layer_bytes + kvb)
             ops.lib().attn_fwd_q8_shards(q, kv_ptrs, sc_ptrs, self.n_rows, [0] * self.world, [0] * self.world, o, None,
-                                         list(lq), list(lkv), list(ls), list(lq), E, H, T * H, nq, D,
+                                         list(lq), list(lkv), list(ls), list(lq), A, H, T * H, nq, Dp,
                                          1.0 / math.sqrt(D))
             x = ops.gemm_residual(o, wb["wo_cross"], x, layer.alpha, w_kn=True)
             wq = {"wb": wb}
