@@ -36,13 +36,15 @@ void attn_fwd_q8(const torch::Tensor& q, const torch::Tensor& kv, const torch::T
                  int64_t Nk, int64_t d_valid, double scale);
 torch::Tensor qass_fwd(const torch::Tensor& q, const torch::Tensor& s, const c10::optional<torch::Tensor>& w1,
                        const c10::optional<torch::Tensor>& b1, const c10::optional<torch::Tensor>& w2,
-                       const c10::optional<torch::Tensor>& b2, int64_t H, int64_t D);
+                       const c10::optional<torch::Tensor>& b2, int64_t H, int64_t D,
+                       const c10::optional<torch::Tensor>& status);
 torch::Tensor qass_bwd(const torch::Tensor& q, const torch::Tensor& dout, const torch::Tensor& s,
                        const c10::optional<torch::Tensor>& w1, const c10::optional<torch::Tensor>& b1,
                        const c10::optional<torch::Tensor>& w2, const c10::optional<torch::Tensor>& b2,
                        torch::Tensor& gs, const c10::optional<torch::Tensor>& gw1,
                        const c10::optional<torch::Tensor>& gb1, const c10::optional<torch::Tensor>& gw2,
-                       const c10::optional<torch::Tensor>& gb2, int64_t H, int64_t D, const c10::optional<torch::Tensor>& out);
+                       const c10::optional<torch::Tensor>& gb2, int64_t H, int64_t D, const c10::optional<torch::Tensor>& out,
+                       const c10::optional<torch::Tensor>& status);
 torch::Tensor exp2_poly_eval(const torch::Tensor& x);
 std::vector<torch::Tensor> ln_act_fwd(const torch::Tensor& x, const c10::optional<torch::Tensor>& gamma,
                                       const c10::optional<torch::Tensor>& beta, double eps, int64_t act);
@@ -175,8 +177,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_ipc_open", &nori::peer_ipc_open);
   m.def("peer_ipc_close", &nori::peer_ipc_close);
   m.def("tensor_from_ptr", &nori::tensor_from_ptr);
-  m.def("qass_fwd", &nori::qass_fwd);
-  m.def("qass_bwd", &nori::qass_bwd);
+  m.def("qass_fwd", &nori::qass_fwd, pybind11::arg("q"), pybind11::arg("s"), pybind11::arg("w1"), pybind11::arg("b1"), pybind11::arg("w2"),
+        pybind11::arg("b2"), pybind11::arg("H"), pybind11::arg("D"), pybind11::arg("status") = pybind11::none());
+  m.def("qass_bwd", &nori::qass_bwd, pybind11::arg("q"), pybind11::arg("dout"), pybind11::arg("s"), pybind11::arg("w1"), pybind11::arg("b1"),
+        pybind11::arg("w2"), pybind11::arg("b2"), pybind11::arg("gs"), pybind11::arg("gw1"), pybind11::arg("gb1"), pybind11::arg("gw2"), pybind11::arg("gb2"),
+        pybind11::arg("H"), pybind11::arg("D"), pybind11::arg("out"), pybind11::arg("status") = pybind11::none());
   m.def("rms_apply", &nori::rms_apply);
   m.def("swiglu_bwd", &nori::swiglu_bwd);
   m.def("rms_bwd", &nori::rms_bwd);

@@ -13,6 +13,10 @@
 // gradient buffer) and reduces ds [H, D], db1, db2, dW1, dW2 across all vectors:
 // every 128 vectors the CTA stages (dz2, gelu) and (dz1, q) in shared memory and four
 // warps each accumulate a 16-row slice of dW2 and dW1 on the tensor cores.
+//
+// With the gate MLP and 128 % H == 0, H <= 16, both entry points run the tcgen05 kernels
+// of qass_tc.cu instead (environment NORI_QASS_TC=0 selects these for comparison); the
+// kernels below serve the other head counts and the gate-free modes.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -578,6 +582,18 @@ __global__ void __launch_bounds__(kThreads) qass_bwd_kernel(Params p) {
 
 }  // namespace qass
 
+// tensor-core kernels (qass_tc.cu)
+bool qass_tc_supported(int64_t H, int64_t D);
+void qass_tc_launch(bool bwd, const torch::Tensor& q, const torch::Tensor* dout, torch::Tensor& out,
+                    const float* s, const float* w1, const float* b1, const float* w2, const float* b2, float* gs,
+                    float* gw1, float* gb1, float* gw2, float* gb2, int64_t H, int64_t D, int* status);
+
+static int* opt_status(const c10::optional<torch::Tensor>& st) {
+  if (!st.has_value() || !st->defined()) return nullptr;
+  TORCH_CHECK(st->is_cuda() && st->scalar_type() == at::kInt && st->numel() >= 1, "qass: int32 status word");
+  return st->data_ptr<int>();
+}
+
 static int sm_count(int dev) {
   int n = 0;
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
@@ -595,7 +611,8 @@ static void check_q(const torch::Tensor& q, int64_t H, int64_t D) {
 // q' = q * s * (1 + tanh(gate(q))) (gate optional) -> new [R, H*D] bf16
 torch::Tensor qass_fwd(const torch::Tensor& q, const torch::Tensor& s, const c10::optional<torch::Tensor>& w1,
                        const c10::optional<torch::Tensor>& b1, const c10::optional<torch::Tensor>& w2,
-                       const c10::optional<torch::Tensor>& b2, int64_t H, int64_t D) {
+                       const c10::optional<torch::Tensor>& b2, int64_t H, int64_t D,
+                       const c10::optional<torch::Tensor>& status) {
   check_q(q, H, D);
   const at::cuda::CUDAGuard guard(q.device());
   auto out = torch::empty({q.size(0), H * D}, q.options());
@@ -624,6 +641,11 @@ torch::Tensor qass_fwd(const torch::Tensor& q, const torch::Tensor& s, const c10
   p.H = static_cast<int>(H);
   p.D = static_cast<int>(D);
   if (p.R == 0) return out;
+  if (p.gate && qass_tc_supported(H, D)) {
+    qass_tc_launch(false, q, nullptr, out, p.s, p.w1, p.b1, p.w2, p.b2, nullptr, nullptr, nullptr, nullptr, nullptr,
+                   H, D, opt_status(status));
+    return out;
+  }
   if (!p.gate) {
     // the gate-free path still stages (zero) weights: give it valid pointers
     w1c = torch::zeros({64, D}, q.options().dtype(torch::kFloat));
@@ -652,7 +674,7 @@ torch::Tensor qass_bwd(const torch::Tensor& q, const torch::Tensor& dout, const 
                        torch::Tensor& gs, const c10::optional<torch::Tensor>& gw1,
                        const c10::optional<torch::Tensor>& gb1, const c10::optional<torch::Tensor>& gw2,
                        const c10::optional<torch::Tensor>& gb2, int64_t H, int64_t D,
-                       const c10::optional<torch::Tensor>& out) {
+                       const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& status) {
   check_q(q, H, D);
   TORCH_CHECK(dout.scalar_type() == at::kFloat && dout.dim() == 2 && dout.stride(1) == 1 && dout.size(0) == q.size(0),
               "qass_bwd: fp32 [R, H*D] gradient");
@@ -708,6 +730,15 @@ torch::Tensor qass_bwd(const torch::Tensor& q, const torch::Tensor& dout, const 
   p.H = static_cast<int>(H);
   p.D = static_cast<int>(D);
   if (p.R == 0) return dq;
+  if (p.gate && qass_tc_supported(H, D)) {
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(dq.data_ptr()) % 16 == 0 && dq.stride(0) % 8 == 0,
+                "qass_bwd: the tensor-core kernel writes 16-byte row chunks of dq");
+    TORCH_CHECK(gb2->numel() >= D && gb1->numel() >= 64 && gw1->numel() >= 64 * D && gw2->numel() >= D * 64,
+                "qass_bwd: weight-gradient accumulator shapes");
+    qass_tc_launch(true, q, &dout, dq, p.s, p.w1, p.b1, p.w2, p.b2, p.gs, p.gw1, p.gb1, p.gw2, p.gb2, H, D,
+                   opt_status(status));
+    return dq;
+  }
   const int64_t steps = (p.R * p.H + qass::kStageVec - 1) / qass::kStageVec;
   const int blocks = static_cast<int>(std::min<int64_t>(steps, sm_count(q.get_device()) * 2));
   const int dyn = 4 * qass::kStageVec * 128 + qass::kWarps * 2 * 16 * 128 +

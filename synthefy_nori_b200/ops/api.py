@@ -203,14 +203,15 @@ def dequantize_int8(q: torch.Tensor, scale: torch.Tensor, out: torch.Tensor | No
 
 def qass_fwd(q, s, w1=None, b1=None, w2=None, b2=None, *, H: int, D: int):
     """``q * s * (1 + tanh(W2 gelu(W1 q + b1) + b2))`` per head vector (gate optional)."""
-    return _lib().qass_fwd(q, s, w1, b1, w2, b2, int(H), int(D))
+    return _lib().qass_fwd(q, s, w1, b1, w2, b2, int(H), int(D), status_word(q.device))
 
 
 def qass_bwd(q, dout, s, gs, w1=None, b1=None, w2=None, b2=None, gw1=None, gb1=None, gw2=None, gb2=None, *, H: int,
              D: int, out=None):
     """Backward of ``qass_fwd``: returns dq (bf16; written into ``out`` when given, e.g. the
     query columns of a fused Q/K/V gradient); accumulates ds and the gate-MLP grads."""
-    return _lib().qass_bwd(q, dout, s, w1, b1, w2, b2, gs, gw1, gb1, gw2, gb2, int(H), int(D), out)
+    return _lib().qass_bwd(q, dout, s, w1, b1, w2, b2, gs, gw1, gb1, gw2, gb2, int(H), int(D), out,
+                           status_word(q.device))
 
 
 def quantile_decode(pred: torch.Tensor, taus: torch.Tensor, levels=None, return_sorted: bool = False):
