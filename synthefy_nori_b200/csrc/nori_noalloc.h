@@ -40,8 +40,9 @@ extern "C" {
 // (nori_attention_bwd_noalloc_error() then gives a one-line reason). Every check runs
 // before any work is queued, so a rejected call leaves dq, dk, dv and the scratch alone.
 // The first call on each device looks up the scratch array's device address with
-// cudaGetSymbolAddress; make that first call before any stream capture. Every call on a device shares the one scratch array and overwrites
-// it, so calls that may overlap on the GPU (different streams without ordering) race.
+// cudaGetSymbolAddress (once per device; later calls reuse it). Every call on a device
+// shares the one scratch array and overwrites it, so calls that may overlap on the GPU
+// (different streams without ordering) race.
 cudaError_t nori_attention_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout,
                                        const float* lse, float* dq, void* dk, void* dv, const int64_t* lq,
                                        const int64_t* lk, const int64_t* lv, const int64_t* lo, const int64_t* ldo,
