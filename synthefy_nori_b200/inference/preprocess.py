@@ -128,6 +128,77 @@ class QuantileMap:
         return torch.where(torch.isnan(x), x.double(), u).to(x.dtype)
 
 
+class KernelDensityIntegral:
+    """Kernel-density-integral transform per column (McCarter, "The Kernel Density Integral
+    Transformation", TMLR 2023), restated here from the paper: the CDF of a Gaussian kernel
+    density estimate of the (NaN-free, NaN -> column mean) context values,
+
+        F(x) = mean_i Phi((x - x_i) / h),   h = alpha * std(x),
+
+    rescaled so the column minimum maps to 0 and the maximum to 1. Small ``alpha`` tends
+    to the quantile transform, large ``alpha`` to min-max scaling. F is evaluated on a grid
+    of ``n_grid`` points over [min, max] (one batched tensor op for all columns) and
+    interpolated; ``output="normal"`` applies the normal quantile function to the result.
+    Reference worker tags: ``kdi_uni`` / ``kdi_norm`` / ``kdi_*_alpha_<a>`` /
+    ``norm_and_kdi`` (``inference/preprocess.py:1104-1150`` of the reference)."""
+
+    def __init__(self, alpha: float = 1.0, output: str = "uniform", n_grid: int = 1024, chunk: int = 4096):
+        if output not in ("uniform", "normal"):
+            raise ValueError(f"unknown KDI output distribution {output!r}")
+        self.alpha, self.output, self.n_grid, self.chunk = float(alpha), output, int(n_grid), int(chunk)
+
+    def fit(self, x: torch.Tensor) -> "KernelDensityIntegral":
+        xd = x.double()
+        mean = _col_nanmean(xd)
+        xd = _nan_fill_mean(xd, mean)
+        n, p = xd.shape
+        lo = xd.min(0).values if n else xd.new_zeros(p)
+        hi = xd.max(0).values if n else xd.new_ones(p)
+        sd = xd.std(0, unbiased=True) if n > 1 else xd.new_zeros(p)
+        h = (self.alpha * sd).clamp_min(1e-12)
+        t = torch.linspace(0, 1, self.n_grid, device=x.device, dtype=torch.float64)
+        grid = lo[None] + t[:, None] * (hi - lo)[None]  # [G, p]
+        cdf = xd.new_zeros(self.n_grid, p)
+        for i in range(0, n, self.chunk):  # mean of Phi over the context values, in row chunks
+            z = (grid[:, None, :] - xd[None, i : i + self.chunk, :]) / h
+            cdf += torch.special.ndtr(z).sum(1)
+        cdf /= max(n, 1)
+        span = cdf[-1] - cdf[0]
+        u = (cdf - cdf[0]) / torch.where(span > 0, span, torch.ones_like(span))
+        const = (hi - lo) <= 0
+        self.grid_ = torch.where(const[None], lo[None] + t[:, None], grid)
+        self.u_ = torch.where(const[None], torch.full_like(u, 0.5), torch.cummax(u, 0).values)
+        self.mean_ = mean
+        return self
+
+    def transform(self, x: torch.Tensor) -> torch.Tensor:
+        xd = _nan_fill_mean(x.double(), self.mean_)
+        u = _interp(xd, self.grid_, self.u_)
+        if self.output == "normal":
+            u = torch.special.ndtri(u.clamp(1e-7, 1 - 1e-7))
+        return u.to(x.dtype)
+
+
+def _kdi_worker(tag: str) -> "KernelDensityIntegral | None":
+    """The reference's KDI worker tags -> a transform (None for other tags)."""
+    if tag in ("kdi_uni", "kdi_norm"):
+        return KernelDensityIntegral(1.0, "uniform" if tag == "kdi_uni" else "normal")
+    for prefix, out in (("kdi_uni_alpha_", "uniform"), ("kdi_norm_alpha_", "normal")):
+        if tag.startswith(prefix):
+            return KernelDensityIntegral(float(tag[len(prefix):]), out)
+    return None
+
+
+class _Union:
+    """Columns of several fitted transforms side by side (FeatureUnion)."""
+
+    def __init__(self, parts):
+        self.parts = parts
+
+    def transform(self, x: torch.Tensor) -> torch.Tensor:
+        return torch.cat([w.transform(x) for w in self.parts], 1)
+
+
 class HighDimFeatureSelector(Step):
     def __init__(self, strategy: str = "svd_all", top_k: int = 256, n_features_threshold: int = 128,
                  binary_threshold: float = 0.5, svd_components: int = 64, svd_rows_per_component: int = 1,
@@ -424,6 +495,11 @@ class RebalanceFeatureDistribution(Step):
                 w = ("affine", med, torch.where(iqr > 0, iqr, torch.ones_like(iqr)))
             elif tag is None:
                 w = None
+            elif tag == "norm_and_kdi":
+                w = _Union([QuantileMap(max(n // 10, 2), "normal").fit(xt),
+                            KernelDensityIntegral(1.0, "uniform").fit(xt)])
+            elif _kdi_worker(tag) is not None:
+                w = _kdi_worker(tag).fit(xt)
             else:
                 raise ValueError(f"worker tag {tag!r} is not provided by this build")
             self.workers_.append(w)
