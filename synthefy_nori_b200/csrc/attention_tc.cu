@@ -16,8 +16,10 @@
 //               PV_0, S_2, PV_1, S_3, ... so a score tile is always in flight;
 //   warps 4..7 / 8..11  two softmax groups, one per key-tile parity, each with its own
 //               running max / sum: thread = query row (its TMEM lane), all 128 columns;
-//               P_j (bf16) goes to shared memory in the 128B-swizzled K-major layout the
-//               MMA reads.  The max is lazy (O_g is rescaled in TMEM only when a row's
+//               P_j (bf16 pairs) is stored back over the first 64 columns of its own score
+//               buffer in TMEM, and the P . V MMA takes its A operand from there (no
+//               shared-memory round trip for P: the tensor cores read only V from shared
+//               memory for that product).  The max is lazy (O_g is rescaled in TMEM only when a row's
 //               max grows by more than 2^8), and the groups merge their (max, sum,
 //               O_g) once per item.  The two groups work on different tiles at the same
 //               time, so one group's waits overlap the other's arithmetic.
@@ -48,11 +50,11 @@ constexpr int kSoftmaxWarps = 8;  // softmax-side barriers take one arrive per w
 constexpr uint32_t kRegsLow = 48, kRegsSoftmax = 224;
 static_assert(4 * 32 * kRegsLow + 8 * 32 * kRegsSoftmax <= kThreads * 168, "register split over the launch total");
 constexpr int kTileBytes = kM * kD * 2;  // 16 KB (Q, K or V tile)
-constexpr int kPBytes = kM * kN * 2;     // 32 KB (P tile: two 64-key panels)
 constexpr int kStages = 3;  // K and V rings (separate: K(j) frees after S_j, V(j) after O_j)
-// smem: Q[2] | K[3] | V[3] | P[2] | barriers
-constexpr int kSmemBytes = kTileBytes * (2 + 2 * kStages) + kPBytes * 2 + 1024 + 256;
-constexpr uint32_t kTmemCols = 512;  // S[2] (2 x 128) + O[item parity][group] (4 x 64)
+// smem: Q[2] | K[3] | V[3] | barriers
+constexpr int kSmemBytes = kTileBytes * (2 + 2 * kStages) + 1024 + 256;
+// S[2] (2 x 128; P_j overwrites the first 64 columns of its S buffer) + O[item parity][group] (4 x 64)
+constexpr uint32_t kTmemCols = 512;
 }  // namespace fa
 
 struct AttnTcParams {
@@ -230,8 +232,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   uint8_t* sQ = smem;                             // 2 buffers (consecutive work items)
   uint8_t* sK = sQ + 2 * kTileBytes;              // kStages
   uint8_t* sV = sK + kStages * kTileBytes;        // kStages
-  uint8_t* sP = sV + kStages * kTileBytes;        // one 32 KB P tile per softmax group
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kStages * kTileBytes);
   uint64_t* q_full = bars;        // [2]
   uint64_t* q_empty = bars + 2;   // [2]
   uint64_t* s_full = bars + 4;    // [group]
@@ -376,13 +377,14 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
           const int st = static_cast<int>(gv % kStages);
           if (!(ok = mbar_wait(&v_full[st], (gv / kStages) & 1, p.status, kTimeoutMma, abort_flag))) break;
           tc_fence_after();
-          const uint32_t aP = smem_u32(sP + grp * kPBytes);
           const uint32_t bV = smem_u32(sV + st * kTileBytes);
+          // A = P_j from TMEM (8 columns of bf16 pairs per 16 keys); this MMA is issued before
+          // the group's next score MMA, which overwrites the same columns, and tcgen05.mma of
+          // one thread execute in issue order
 #pragma unroll
           for (int k = 0; k < kN / 16; ++k) {
-            const uint64_t da = umma_desc_kmajor_sw128(aP + (k >> 2) * (kM * 128) + (k & 3) * 32);
             const uint64_t db = umma_smem_desc(bV + k * 2048, 8192, 1024, 2);
-            umma_bf16_ss(tO + (qb * 2 + grp) * kD, da, db, idesc_o, (k > 0 || !first) ? 1u : 0u);
+            umma_bf16_ts(tO + (qb * 2 + grp) * kD, tS + grp * kN + k * 8, db, idesc_o, (k > 0 || !first) ? 1u : 0u);
           }
           umma_commit(&o_full[grp]);
           umma_commit(&v_empty[st]);
@@ -413,7 +415,6 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
     const int r = q * 32 + lane;  // row in tile == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t tSg = tS + grp * kN + lane_off;
-    uint8_t* const Pg = sP + grp * kPBytes;
     bool ok = true;
     int64_t cnt = 0;  // this group's tiles so far (barrier completions)
     int it = 0;
@@ -441,8 +442,9 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         float mx = rowmax64(va, vb, valid);
         if (valid > 64) mx = fmaxf(mx, rowmax64(vc, vd, valid - 64));
         const float m_cand = mx * p.scale_log2;
-        // the group's previous P . V (same P buffer, same accumulator) must be complete
-        // before P is overwritten or O rescaled
+        // the group's previous P . V (same accumulator) must be complete before O is
+        // rescaled (it is: s_full of this tile was committed after it; the wait also orders
+        // the accumulator reads below)
         if (cnt > 0 && !mbar_wait_warp(&o_full[grp], (cnt - 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) {
           ok = false;
           break;
@@ -456,31 +458,20 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
           m_used = m_cand;
           need = true;
         }
-        // P (bf16) into the two 64-key panels, 128B-swizzled K-major
+        // P (bf16 pairs) over the first 64 columns of this group's score buffer: keys
+        // 32c .. 32c + 31 go to columns 16c .. 16c + 15 (the whole row is in registers already)
         const float nm = -m_used;
         float rsum = 0.f;
         {
           uint32_t pk[16];
           rsum += softmax_chunk32(va, valid, p.scale_log2, nm, pk);
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc)
-            *reinterpret_cast<uint4*>(Pg + r * 128 + ((cc ^ (r & 7)) << 4)) =
-                make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+          tmem_st16(tSg, pk);
           rsum += softmax_chunk32(vb, valid - 32, p.scale_log2, nm, pk);
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc)
-            *reinterpret_cast<uint4*>(Pg + r * 128 + (((4 + cc) ^ (r & 7)) << 4)) =
-                make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+          tmem_st16(tSg + 16, pk);
           rsum += softmax_chunk32(vc, valid - 64, p.scale_log2, nm, pk);
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc)
-            *reinterpret_cast<uint4*>(Pg + kM * 128 + r * 128 + ((cc ^ (r & 7)) << 4)) =
-                make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+          tmem_st16(tSg + 32, pk);
           rsum += softmax_chunk32(vd, valid - 96, p.scale_log2, nm, pk);
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc)
-            *reinterpret_cast<uint4*>(Pg + kM * 128 + r * 128 + (((4 + cc) ^ (r & 7)) << 4)) =
-                make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+          tmem_st16(tSg + 48, pk);
         }
         // O_g rescale after P left the registers (warp-collective TMEM read-modify-write;
         // lanes that keep their max scale by 1)
@@ -499,7 +490,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         }
         l = l * a;
         l += rsum;
-        fence_proxy_async_smem();
+        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[grp]);
@@ -571,8 +562,9 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
 //   S^T  = K Q^T     (M=128 keys, N=128 q, K=64)   -> TMEM
 //   dP^T = V dO^T    (M=128 keys, N=128 q, K=64)   -> TMEM
 //   softmax warps (thread = key row, two warps per lane quarter split the q columns):
-//     P^T = exp2(S^T scale log2e - LSE log2e), dS^T = P^T (dP^T - Dvec) -> bf16, smem
-//   dV += P^T dO     (M=128 keys, N=64, K=128 q; dO read MN-major)
+//     P^T = exp2(S^T scale log2e - LSE log2e) -> bf16 pairs into 64 TMEM columns,
+//     dS^T = P^T (dP^T - Dvec) -> bf16, smem
+//   dV += P^T dO     (M=128 keys, N=64, K=128 q; A = P^T from TMEM, dO read MN-major)
 //   dK += dS^T Q     (M=128 keys, N=64, K=128 q; Q read MN-major)
 //   dQ  = dS K       (M=128 q, N=64, K=128 keys; dS^T read MN-major as A, K MN-major)
 //   the softmax warps drain dQ (thread = query row) into a 4 KB shared-memory slot per
@@ -584,10 +576,11 @@ constexpr int kThreads = 384;  // warps 0 (TMA), 1 (MMA), 4..11 (softmax / drain
 constexpr int kWarpsSm = 8;
 constexpr int kTile = kM * kD * 2;      // 16 KB
 constexpr int kPanel = kM * 128;        // 16 KB: 128 rows x 64 bf16
-// smem: K | V | Q[2] | dO[2] | P^T (2 panels) | dS^T (2 panels) | dQ staging (8 x 4 KB) | barriers
+// smem: K | V | Q[2] | dO[2] | dS^T (2 panels) | dQ staging (8 x 4 KB) | barriers
 constexpr int kDQStage = 32 * 128;      // 4 KB per drain warp: 32 query rows x 32 fp32 (128B-swizzled)
-constexpr int kSmemBytes = kTile * 6 + 4 * kPanel + kWarpsSm * kDQStage + 1024 + 256;
-constexpr uint32_t kTmemCols = 512;  // S 0..127, dP 128..255, dV 256..319, dK 320..383, dQ 384..447
+constexpr int kSmemBytes = kTile * 6 + 2 * kPanel + kWarpsSm * kDQStage + 1024 + 256;
+// S 0..127, dP 128..255, dV 256..319, dK 320..383, dQ 384..447, P^T (bf16 pairs) 448..511
+constexpr uint32_t kTmemCols = 512;
 }  // namespace fb
 
 struct AttnBwdTcParams {
@@ -619,8 +612,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
   uint8_t* sV = sK + kTile;
   uint8_t* sQ = sV + kTile;        // 2 stages
   uint8_t* sDO = sQ + 2 * kTile;   // 2 stages
-  uint8_t* sP = sDO + 2 * kTile;   // 2 panels
-  uint8_t* sDS = sP + 2 * kPanel;  // 2 panels
+  uint8_t* sDS = sDO + 2 * kTile;  // 2 panels
   uint8_t* sDQ = sDS + 2 * kPanel; // dQ staging, one 4 KB slot per drain warp
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDQ + kWarpsSm * kDQStage);
   uint64_t* kv_full = bars;        // [1] (index 1 unused)
@@ -670,6 +662,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
+  const uint32_t tPT = tmem + 448;  // P^T: key row = lane, queries 2c, 2c + 1 in column c
 
   // work item w -> (head bh, key tile); items are visited with stride gridDim.x
   auto item_coords = [&](int64_t w, int& k0, int& i2, int& i1, int& i0, int64_t& bh) {
@@ -731,7 +724,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       constexpr uint32_t id_s = umma_idesc_bf16(kM, kM, false, false);    // S^T, dP^T
       constexpr uint32_t id_kv = umma_idesc_bf16(kM, kD, false, true);    // dV, dK: A K-major, B MN-major
       constexpr uint32_t id_q = umma_idesc_bf16(kM, kD, true, true);      // dQ: A (dS) MN-major, B (K) MN-major
-      const uint32_t aP = smem_u32(sP), aDS = smem_u32(sDS);
+      const uint32_t aDS = smem_u32(sDS);
       int64_t gq = 0;  // global query-block counter: Q / dO stage and the S / P / dQ barrier phases
       int it = 0;
       bool ok = true;
@@ -767,10 +760,10 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
           const uint32_t aQ = smem_u32(sQ + s * kTile), aDO = smem_u32(sDO + s * kTile);
 #pragma unroll
           for (int k = 0; k < kM / 16; ++k) {
-            // K-major A over q: panel (k >> 2), 32-byte steps; MN-major B over q rows: 2048-byte steps
-            const uint64_t dP = umma_desc_kmajor_sw128(aP + (k >> 2) * kPanel + (k & 3) * 32);
+            // A = P^T from TMEM, 8 columns per 16 queries; dS^T K-major A over q: panel (k >> 2),
+            // 32-byte steps; MN-major B over q rows: 2048-byte steps
             const uint64_t dS = umma_desc_kmajor_sw128(aDS + (k >> 2) * kPanel + (k & 3) * 32);
-            umma_bf16_ss(tDV, dP, umma_smem_desc(aDO + k * 2048, 8192, 1024, 2), id_kv, (j > 0 || k > 0));
+            umma_bf16_ts(tDV, tPT + k * 8, umma_smem_desc(aDO + k * 2048, 8192, 1024, 2), id_kv, (j > 0 || k > 0));
             umma_bf16_ss(tDK, dS, umma_smem_desc(aQ + k * 2048, 8192, 1024, 2), id_kv, (j > 0 || k > 0));
           }
 #pragma unroll
@@ -865,7 +858,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
           break;
         }
         const int qbase = j * kM + half * 64;
-        uint8_t* panelP = sP + half * kPanel;
+        const uint32_t tPw = tPT + lane_off + half * 32;  // this warp's 64 queries: 32 columns
         uint8_t* panelS = sDS + half * kPanel;
         if (key_ok && qbase + 64 <= p.Nq) {
           // every column valid: scaling, the polynomial 2^x (half of the columns; the other
@@ -902,7 +895,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
               dk4[2 * h] = pack_bf16x2(d0, d1);
               dk4[2 * h + 1] = pack_bf16x2(d2, d3);
             }
-            *reinterpret_cast<uint4*>(panelP + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            tmem_st4(tPw + ch * 4, pk[0], pk[1], pk[2], pk[3]);
             *reinterpret_cast<uint4*>(panelS + r * 128 + ((ch ^ (r & 7)) << 4)) =
                 make_uint4(dk4[0], dk4[1], dk4[2], dk4[3]);
           }
@@ -928,12 +921,13 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
               pk[i2p] = pack_bf16x2(pe[0], pe[1]);
               dk4[i2p] = pack_bf16x2(de[0], de[1]);
             }
-            *reinterpret_cast<uint4*>(panelP + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            tmem_st4(tPw + ch * 4, pk[0], pk[1], pk[2], pk[3]);
             *reinterpret_cast<uint4*>(panelS + r * 128 + ((ch ^ (r & 7)) << 4)) =
                 make_uint4(dk4[0], dk4[1], dk4[2], dk4[3]);
           }
         }
         fence_proxy_async_smem();
+        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full);
@@ -986,46 +980,6 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host
-namespace {
-
-struct Map5 {
-  CUtensorMap map;
-  int pos[4];  // positions of row, i2, i1, i0
-};
-
-// Layout (s0, s1, s2, row, d1, d2) of a [.., rows, d] view -> 5-D map with the non-contiguous
-// dimensions sorted by stride (the box is 64 x 1 x .. x 128 rows x ..).
-Map5 make_map(const torch::Tensor& t, const std::vector<int64_t>& l, int64_t n_rows, int64_t n_i0, int d_valid,
-              int elem_bytes = 2, int box_cols = fa::kD, int box_rows = fa::kM,
-              CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
-  struct Dim {
-    int64_t extent, stride;
-    int role;  // 0 row, 1 i2, 2 i1, 3 i0
-  };
-  const int64_t d1 = l[4], d2 = l[5];
-  std::array<Dim, 4> dims = {Dim{n_rows, l[3], 0}, Dim{d2, l[2], 1}, Dim{d1, l[1], 2}, Dim{n_i0, l[0], 3}};
-  // dimensions of extent 1 get a harmless stride (never stepped)
-  int64_t big = 1;
-  for (auto& d : dims) big = std::max(big, d.stride * std::max<int64_t>(d.extent, 1));
-  for (auto& d : dims)
-    if (d.extent <= 1 || d.stride == 0) d.stride = big;
-  std::stable_sort(dims.begin(), dims.end(), [](const Dim& a, const Dim& b) { return a.stride < b.stride; });
-  int64_t ext[5], strides[4];
-  int box[5];
-  ext[0] = d_valid;
-  box[0] = box_cols;
-  Map5 m{};
-  for (int i = 0; i < 4; ++i) {
-    ext[i + 1] = std::max<int64_t>(dims[i].extent, 1);
-    strides[i] = dims[i].stride * elem_bytes;
-    box[i + 1] = dims[i].role == 0 ? box_rows : 1;
-    m.pos[dims[i].role] = i + 1;
-  }
-  m.map = make_tmap_nd_bf16(t.data_ptr(), 5, ext, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, dtype);
-  return m;
-}
-
-}  // namespace
 
 void attn_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
                  const c10::optional<torch::Tensor>& lse, std::vector<int64_t> lq, std::vector<int64_t> lk,

@@ -30,6 +30,16 @@ void attn_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
                  const c10::optional<torch::Tensor>& lse, std::vector<int64_t> lq, std::vector<int64_t> lk,
                  std::vector<int64_t> lv, std::vector<int64_t> lo, int64_t BH, int64_t Nq, int64_t Nk, int64_t d_valid,
                  double scale, const torch::Tensor& status);
+bool attn_feat_tc_supported(int64_t T, int64_t d_valid);
+void attn_feat_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
+                      const c10::optional<torch::Tensor>& lse, std::vector<int64_t> lq, std::vector<int64_t> lk,
+                      std::vector<int64_t> lv, std::vector<int64_t> lo, int64_t BH, int64_t T, int64_t d_valid,
+                      double scale, const torch::Tensor& status);
+void attn_feat_bwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& o,
+                      const torch::Tensor& dout, const torch::Tensor& lse, torch::Tensor& dq, torch::Tensor& dk,
+                      torch::Tensor& dv, std::vector<int64_t> lq, std::vector<int64_t> lkv, std::vector<int64_t> lo,
+                      std::vector<int64_t> lg, int64_t BH, int64_t T, int64_t d_valid, double scale,
+                      const torch::Tensor& status);
 void attn_fwd_q8(const torch::Tensor& q, const torch::Tensor& kv, const torch::Tensor& scales, torch::Tensor& o,
                  const c10::optional<torch::Tensor>& lse, std::vector<int64_t> lq, std::vector<int64_t> lkv,
                  std::vector<int64_t> ls, std::vector<int64_t> lo, int64_t E, int64_t H, int64_t BH, int64_t Nq,
@@ -145,6 +155,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &nori::attn_bwd);
   m.def("attn_fwd_tc", &nori::attn_fwd_tc);
   m.def("attn_fwd_q8", &nori::attn_fwd_q8);
+  m.def("attn_feat_tc_supported", &nori::attn_feat_tc_supported);
+  m.def("attn_feat_fwd_tc", &nori::attn_feat_fwd_tc);
+  m.def("attn_feat_bwd_tc", &nori::attn_feat_bwd_tc);
   m.def("attn_bwd_tc", &nori::attn_bwd_tc);
   m.def("attn_dvec", &nori::attn_dvec);
   m.def("attn_fwd_q8_shards", &nori::attn_fwd_q8_shards);

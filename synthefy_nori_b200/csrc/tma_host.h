@@ -7,7 +7,10 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <algorithm>
+#include <array>
 #include <mutex>
+#include <vector>
 
 namespace nori {
 
@@ -74,6 +77,46 @@ inline CUtensorMap make_tmap_nd_bf16(void* base, int rank, const int64_t* dims, 
                                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (rank ", rank, ") failed with code ", static_cast<int>(r));
+  return m;
+}
+
+// A strided [.., rows, d] view given as the layout (s0, s1, s2, row, d1, d2) (element
+// strides of the i0 / i1 / i2 / row indices; bh -> (i0, i1, i2) with i2 fastest) -> 5-D map
+// with the non-contiguous dimensions sorted by stride. The box is box_cols x 1 x .. x
+// box_rows rows x ..; the contiguous dimension has extent d_valid, so columns past it (head
+// padding) and rows past n_rows read as zero.
+struct Map5 {
+  CUtensorMap map;
+  int pos[4];  // positions of row, i2, i1, i0
+};
+
+inline Map5 make_map(const torch::Tensor& t, const std::vector<int64_t>& l, int64_t n_rows, int64_t n_i0, int d_valid,
+              int elem_bytes = 2, int box_cols = 64, int box_rows = 128,
+              CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
+  struct Dim {
+    int64_t extent, stride;
+    int role;  // 0 row, 1 i2, 2 i1, 3 i0
+  };
+  const int64_t d1 = l[4], d2 = l[5];
+  std::array<Dim, 4> dims = {Dim{n_rows, l[3], 0}, Dim{d2, l[2], 1}, Dim{d1, l[1], 2}, Dim{n_i0, l[0], 3}};
+  // dimensions of extent 1 get a harmless stride (never stepped)
+  int64_t big = 1;
+  for (auto& d : dims) big = std::max(big, d.stride * std::max<int64_t>(d.extent, 1));
+  for (auto& d : dims)
+    if (d.extent <= 1 || d.stride == 0) d.stride = big;
+  std::stable_sort(dims.begin(), dims.end(), [](const Dim& a, const Dim& b) { return a.stride < b.stride; });
+  int64_t ext[5], strides[4];
+  int box[5];
+  ext[0] = d_valid;
+  box[0] = box_cols;
+  Map5 m{};
+  for (int i = 0; i < 4; ++i) {
+    ext[i + 1] = std::max<int64_t>(dims[i].extent, 1);
+    strides[i] = dims[i].stride * elem_bytes;
+    box[i + 1] = dims[i].role == 0 ? box_rows : 1;
+    m.pos[dims[i].role] = i + 1;
+  }
+  m.map = make_tmap_nd_bf16(t.data_ptr(), 5, ext, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, dtype);
   return m;
 }
 

@@ -19,6 +19,9 @@ __all__ = [
     "attention_fwd_tc",
     "attention_fwd_q8",
     "attention_bwd_tc",
+    "attention_feat_fwd_tc",
+    "attention_feat_bwd_tc",
+    "feat_tc_supported",
     "rms_scale",
     "rms_apply",
     "rms_bwd",
@@ -109,6 +112,28 @@ def attention_fwd_tc(q, k, v, o, *, lq, lk, lv, lo, BH, Nq, Nk, d, scale, lse=No
     _lib().attn_fwd_tc(q, k, v, o, lse, _layout(lq), _layout(lk), _layout(lv), _layout(lo), int(BH), int(Nq), int(Nk),
                        int(d), float(scale), status_word(q.device))
     return o
+
+
+def attention_feat_fwd_tc(q, k, v, o, *, lq, lk, lv, lo, BH, T, d, scale, lse=None):
+    """tcgen05 / TMEM feature (within-row) attention forward for rows of at most 64 tokens:
+    two table rows per 128-lane MMA tile. Layouts are feature layouts
+    ``(T * width, *, head stride, width, 1, H)`` (``bh = table row * H + head``)."""
+    _lib().attn_feat_fwd_tc(q, k, v, o, lse, _layout(lq), _layout(lk), _layout(lv), _layout(lo), int(BH), int(T),
+                            int(d), float(scale), status_word(q.device))
+    return o
+
+
+def attention_feat_bwd_tc(q, k, v, o, do, lse, dq, dk, dv, *, lq, lkv, lo, lg, BH, T, d, scale):
+    """tcgen05 / TMEM feature-attention backward (two table rows per item, rows of at most
+    64 tokens): dQ, dK, dV written once in bf16 through the shared layout ``lg``; ``o`` and
+    ``do`` share ``lo``."""
+    _lib().attn_feat_bwd_tc(q, k, v, o, do, lse, dq, dk, dv, _layout(lq), _layout(lkv), _layout(lo), _layout(lg),
+                            int(BH), int(T), int(d), float(scale), status_word(q.device))
+
+
+def feat_tc_supported(T: int, d: int) -> bool:
+    """Whether the tcgen05 feature-attention kernels take rows of ``T`` tokens, head width ``d``."""
+    return bool(_lib().attn_feat_tc_supported(int(T), int(d)))
 
 
 def attention_fwd_q8(q, kv, scales, o, *, lq, lkv, lscale, lo, BH, Nq, Nk, d, scale, lse=None):

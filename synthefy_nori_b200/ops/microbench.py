@@ -2,7 +2,8 @@
 
     python -m synthefy_nori_b200.ops.microbench gemm  --m 131072 --n 1344 --k 448 [--epi store|swiglu|residual|dgrad|wgrad]
     python -m synthefy_nori_b200.ops.microbench attn  --bh 128 --n 2048 --d 56 [--kernel tc|mma|bwd|bwdtc]
-    python -m synthefy_nori_b200.ops.microbench attn  --bh 19200 --n 51 --d 56 --kernel feat|featbwd   (rows x 8 heads)
+    python -m synthefy_nori_b200.ops.microbench attn  --bh 19200 --n 51 --d 56 --kernel feat|featbwd|feattc|featbwdtc
+        (feature attention: --bh table rows, 8 heads each; *tc = the tcgen05 kernels)
     python -m synthefy_nori_b200.ops.microbench qass  --rows 262144 --h 8 --d 56 [--kernel fwd|bwd]
     python -m synthefy_nori_b200.ops.microbench step  --model nori-100m --tables 16 --rows 1200 --ctx 800 --features 100
     python -m synthefy_nori_b200.ops.microbench embed|head|prior|layouts [--model ... --tables --rows --ctx --features]
@@ -75,25 +76,35 @@ def bench_feat_attn(a):
     l3, l1 = (T * 3 * E, 0, D, 3 * E, 1, H), (T * E, 0, D, E, 1, H)
     kw = dict(BH=R * H, Nq=T, Nk=T, d=D, scale=1 / math.sqrt(D))
     flops = 4.0 * R * H * T * T * D
-    fwd = lambda: ops.attention_fwd(y[:, :E], y[:, E : 2 * E], y[:, 2 * E :], o, lq=l3, lk=l3, lv=l3, lo=l1,  # noqa: E731
-                                    lse=lse, **kw)
-    if a.kernel == "feat":
+    tc = a.kernel.endswith("tc")
+    if tc:
+        kwt = dict(BH=R * H, T=T, d=D, scale=1 / math.sqrt(D))
+        fwd = lambda: ops.attention_feat_fwd_tc(y[:, :E], y[:, E : 2 * E], y[:, 2 * E :], o, lq=l3, lk=l3,  # noqa: E731
+                                                lv=l3, lo=l1, lse=lse, **kwt)
+    else:
+        fwd = lambda: ops.attention_fwd(y[:, :E], y[:, E : 2 * E], y[:, 2 * E :], o, lq=l3, lk=l3, lv=l3,  # noqa: E731
+                                        lo=l1, lse=lse, **kw)
+    if a.kernel in ("feat", "feattc"):
         return fwd, flops
     fwd()
     do = torch.randn(R * T, E, device="cuda").to(torch.bfloat16)
     dy = torch.empty(R * T, 3 * E, device="cuda", dtype=torch.bfloat16)
 
     def fn():
-        ops.attention_bwd(y[:, :E], y[:, E : 2 * E], y[:, 2 * E :], o, do, lse, None, dy[:, E : 2 * E],
-                          dy[:, 2 * E :], lq=l3, lk=l3, lv=l3, lo=l1, ldo=l1, ldk=l3, ldv=l3, ldq=l3, dq_bf16=dy[:, :E],
-                          **kw)
+        if tc:
+            ops.attention_feat_bwd_tc(y[:, :E], y[:, E : 2 * E], y[:, 2 * E :], o, do, lse, dy[:, :E],
+                                      dy[:, E : 2 * E], dy[:, 2 * E :], lq=l3, lkv=l3, lo=l1, lg=l3, **kwt)
+        else:
+            ops.attention_bwd(y[:, :E], y[:, E : 2 * E], y[:, 2 * E :], o, do, lse, None, dy[:, E : 2 * E],
+                              dy[:, 2 * E :], lq=l3, lk=l3, lv=l3, lo=l1, ldo=l1, ldk=l3, ldv=l3, ldq=l3,
+                              dq_bf16=dy[:, :E], **kw)
     return fn, flops * 2.5
 
 
 def bench_attn(a):
     from synthefy_nori_b200 import ops
 
-    if a.kernel in ("feat", "featbwd"):
+    if a.kernel in ("feat", "featbwd", "feattc", "featbwdtc"):
         return bench_feat_attn(a)
     BH, N, D = a.bh, a.n, a.d
     q = torch.randn(BH, N, D, device="cuda").to(torch.bfloat16)
