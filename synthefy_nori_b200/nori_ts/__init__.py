@@ -16,6 +16,8 @@ import pandas as pd
 
 from synthefy_nori_b200.nori_ts.features import (AutoSeasonalFeature, CalendarFeature, RunningIndexFeature,
                                                  default_features, seasonal_periods)
+from synthefy_nori_b200.nori_ts.frames import (AdditionalCalendarFeature, FeatureGenerator, FeatureTransformer,
+                                               TimeSeriesDataFrame, generate_test_X)
 
 DEFAULT_QUANTILES = [0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9]
 TARGET = "target"
@@ -93,4 +95,5 @@ class NoriTSForecaster:
 
 
 __all__ = ["NoriTSForecaster", "RunningIndexFeature", "CalendarFeature", "AutoSeasonalFeature", "seasonal_periods",
-           "default_features", "DEFAULT_QUANTILES"]
+           "default_features", "DEFAULT_QUANTILES", "TimeSeriesDataFrame", "generate_test_X", "FeatureGenerator",
+           "FeatureTransformer", "AdditionalCalendarFeature"]
