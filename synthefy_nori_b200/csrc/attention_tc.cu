@@ -860,7 +860,10 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         const int qbase = j * kM + half * 64;
         const uint32_t tPw = tPT + lane_off + half * 32;  // this warp's 64 queries: 32 columns
         uint8_t* panelS = sDS + half * kPanel;
-        if (key_ok && qbase + 64 <= p.Nq) {
+        // the branch is warp-uniform: both paths end in tcgen05.st (a warp-collective store
+        // that every lane must execute together), so a warp whose key rows straddle Nk takes
+        // the per-element path as a whole
+        if (__all_sync(0xffffffffu, key_ok && qbase + 64 <= p.Nq)) {
           // every column valid: scaling, the polynomial 2^x (half of the columns; the other
           // half on the MUFU) and dS = P (dP - D) as packed f32x2
           const uint64_t sc2 = f2pack(p.scale_log2, p.scale_log2);

@@ -15,10 +15,14 @@ runs the encoder stack on its own row shard only:
   buffer only after every peer has copied it (bounded waits);
 * the cross-attention K/V that query rows will use is quantised to int8 (per token and
   head, the reference's absmax rule) into an IPC-shared per-layer cache shard;
-* query rows (split over ranks) run the cached stack; their cross-attention kernel walks
-  the int8 K/V tiles of every rank's shard - peer shards read over NVLink with plain
-  loads and dequantised while staged - so the online softmax covers the whole context in
-  one pass (``attn_fwd_q8_shards``).
+* query rows (split over ranks) run the cached stack; per layer their cross-attention
+  visits the shards one at a time like the context self-attention: the next shard's
+  int8 K/V rows and scales are copied from the owner's memory by the plain-load P2P copy
+  kernel on a side stream into a local double buffer, the current shard is dequantised
+  into one bf16 block and attended by the tcgen05 kernel, and the per-shard outputs are
+  merged by their log-sum-exps (``query_attention="staged"``, the default). The
+  alternative ``"q8_shards"`` runs one mma.sync kernel whose query tiles read every
+  shard's int8 tiles over NVLink directly (no staging memory; ``attn_fwd_q8_shards``).
 
 The reference has no multi-GPU context path: its long-context rungs are single-GPU
 (resident int8, host offload, streamed blocks with an LSE merge, ``model/layer.py:747-934``,
@@ -39,6 +43,7 @@ from synthefy_nori_b200.ops.fused_layer import (
     _cached_bf16,
     _feat_forward,
     _mlp_forward,
+    _attn_mult,
     _qass_apply,
     _seq_layout,
     check_supported,
@@ -97,8 +102,12 @@ class ShardedContextPredictor:
     """Build a row-sharded int8 context cache across the ranks of ``group`` and answer
     queries against it (see module docstring)."""
 
-    def __init__(self, model, device: torch.device, group=None, wait_limit_s: float = 60.0):
+    def __init__(self, model, device: torch.device, group=None, wait_limit_s: float = 60.0,
+                 query_attention: str = "staged"):
         check_supported(model)
+        if query_attention not in ("staged", "q8_shards"):
+            raise ValueError(f"unknown query_attention {query_attention!r}")
+        self.query_attention = query_attention
         self.wait_limit_s = float(wait_limit_s)
         self.model = model.to(device).eval()
         self.device = device
@@ -197,7 +206,7 @@ class ShardedContextPredictor:
                 lkv = _seq_layout(np_, gp, 2 * A)
                 kvb = blk[i % 2]
                 ops.attention_fwd_tc(q, kvb[:, :A], kvb[:, A:], o, lq=lq, lk=lkv, lv=lkv, lo=lq, BH=T * H, Nq=n_loc,
-                                     Nk=np_, d=self.Dp, scale=1.0 / math.sqrt(D), lse=lse)
+                                     Nk=np_, d=self.Dp, scale=_attn_mult(w["info_self"], N) / math.sqrt(D), lse=lse)
                 ops.lib().attn_lse_merge(acc, lse_acc, o, lse, T, H, n_loc, i == 0)
             cur.wait_stream(copy_stream)
             ops.lib().peer_signal(self.flags.ptrs, me, W, step)  # done reading every peer's staging
@@ -207,9 +216,9 @@ class ShardedContextPredictor:
             self.cache.view(base + self.kv_off, R * 2 * A, torch.int8).copy_(q8.reshape(-1))
             self.cache.view(base + self.sc_off, R * 2 * H, torch.float32).copy_(sc.reshape(-1))
             x = ops.gemm_residual(acc.to(BF16), wb["wo_self"], x, layer.alpha, w_kn=True)
-            wq = {"wb": wb}
-            x = _mlp_forward(layer, wq, x)
-            x = _feat_forward(layer, wq, x, g_loc)
+            w["wb"] = wb
+            x = _mlp_forward(layer, w, x)
+            x = _feat_forward(layer, w, x, g_loc)
         # every peer is done with the last staging buffer, then the cache is complete everywhere
         ops.lib().peer_wait(self.flags.ptrs[me], W, W, L, self.wait_limit_s, st)
         torch.cuda.synchronize(self.device)
@@ -228,6 +237,18 @@ class ShardedContextPredictor:
         lq = _seq_layout(nq, g, A)
         lkv = (0, 2 * A, Dp, T * 2 * A, T, H)
         ls = (0, 2 * H, 1, T * 2 * H, T, H)
+        staged = self.query_attention == "staged"
+        if staged:
+            R = x.shape[0]
+            max_rows = max(self.n_rows) * T
+            q8b = [torch.empty(max_rows, 2 * A, device=self.device, dtype=torch.int8) for _ in range(2)]
+            scb = [torch.empty(max_rows, 2 * H, device=self.device, dtype=torch.float32) for _ in range(2)]
+            kvbf = torch.empty(max_rows, 2 * A, device=self.device, dtype=BF16)
+            acc = torch.empty(R, A, device=self.device, dtype=torch.float32)
+            lse_acc = torch.empty(T * H, nq, device=self.device, dtype=torch.float32)
+            lse = torch.empty(T * H, nq, device=self.device, dtype=torch.float32)
+            copy_stream = torch.cuda.Stream(self.device)
+            order = [(self.rank + i) % self.world for i in range(self.world)]  # the local shard first
         for li, layer in enumerate(self.layers):
             w = layer_weights(layer)
             wb = _cached_bf16(layer, w)
@@ -241,13 +262,46 @@ class ShardedContextPredictor:
                 layer_bytes = self.peer_kv_layer_bytes[p][1]
                 kv_ptrs.append(self.cache.ptrs[p] + li * layer_bytes)
                 sc_ptrs.append(self.cache.ptrs[p] + li * layer_bytes + kvb)
-            ops.lib().attn_fwd_q8_shards(q, kv_ptrs, sc_ptrs, self.n_rows, [0] * self.world, [0] * self.world, o, None,
-                                         list(lq), list(lkv), list(ls), list(lq), A, H, T * H, nq, Dp,
-                                         1.0 / math.sqrt(D))
-            x = ops.gemm_residual(o, wb["wo_cross"], x, layer.alpha, w_kn=True)
-            wq = {"wb": wb}
-            x = _mlp_forward(layer, wq, x)
-            x = _feat_forward(layer, wq, x, g)
+            if not staged:
+                ops.lib().attn_fwd_q8_shards(q, kv_ptrs, sc_ptrs, self.n_rows, [0] * self.world, [0] * self.world, o,
+                                             None, list(lq), list(lkv), list(ls), list(lq), A, H, T * H, nq, Dp,
+                                             _attn_mult(w["info_cross"], self.N) / math.sqrt(D))
+                x = ops.gemm_residual(o, wb["wo_cross"], x, layer.alpha, w_kn=True)
+            else:
+                cur = torch.cuda.current_stream(self.device)
+                events = [None, None]
+
+                def fetch(i):
+                    p = order[i]
+                    rp = self.n_rows[p] * T
+                    copy_stream.wait_stream(cur)  # the buffer's previous reader is done
+                    with torch.cuda.stream(copy_stream):
+                        ops.lib().copy_rows(kv_ptrs[p], 2 * A, q8b[i % 2], 2 * A, rp, 2 * A)
+                        ops.lib().copy_rows(sc_ptrs[p], 2 * H * 4, scb[i % 2], 2 * H * 4, rp, 2 * H * 4)
+                        ev = torch.cuda.Event()
+                        ev.record(copy_stream)
+                    events[i % 2] = ev
+
+                fetch(0)
+                for i in range(self.world):
+                    cur.wait_event(events[i % 2])
+                    if i + 1 < self.world:
+                        fetch(i + 1)
+                    np_ = self.n_rows[order[i]]
+                    rp = np_ * T
+                    kv = ops.dequantize_int8(q8b[i % 2][:rp].view(rp, 2, H, Dp), scb[i % 2][:rp].view(rp, 2, H, 1),
+                                             out=kvbf[:rp].view(rp, 2, H, Dp)).view(rp, 2 * A)
+                    gp = Geometry(B=1, ep=np_, nq=0, T=T, E=E, H=H)
+                    lkb = _seq_layout(np_, gp, 2 * A)
+                    ops.attention_fwd_tc(q, kv[:, :A], kv[:, A:], o, lq=lq, lk=lkb, lv=lkb, lo=lq, BH=T * H, Nq=nq,
+                                         Nk=np_, d=Dp, scale=_attn_mult(w["info_cross"], self.N) / math.sqrt(D),
+                                         lse=lse)
+                    ops.lib().attn_lse_merge(acc, lse_acc, o, lse, T, H, nq, i == 0)
+                cur.wait_stream(copy_stream)
+                x = ops.gemm_residual(acc.to(BF16), wb["wo_cross"], x, layer.alpha, w_kn=True)
+            w["wb"] = wb
+            x = _mlp_forward(layer, w, x)
+            x = _feat_forward(layer, w, x, g)
         h = x.view(1, nq, T, E)[:, :, -1]
         return model.decode_regression(model.encoder_out_norm(h.float()))
 

@@ -1,5 +1,7 @@
-"""Context-row-sharded inference (int8 K/V shards in peer memory, multi-shard query
-attention) against the single-GPU int8 context cache, on 2 GPUs (skipped with fewer)."""
+"""Context-row-sharded inference (int8 K/V shards in peer memory; query attention over
+staged, dequantised shards on the tcgen05 kernel with LSE merges, and over the shards
+read in place by the multi-shard int8 kernel) against the single-GPU int8 context cache,
+on 2 and 4 GPUs (skipped with fewer)."""
 
 import os
 
@@ -32,6 +34,8 @@ def _run(rank, world, port, q):
         nq = 100
         lo, hi = rank * nq // world, (rank + 1) * nq // world
         part = sp.predict_raw(x[:, 600 + lo : 600 + hi]).float().cpu()
+        sp.query_attention = "q8_shards"
+        part_q8 = sp.predict_raw(x[:, 600 + lo : 600 + hi]).float().cpu()
         sp.close()
         ref = None
         if rank == 0:
@@ -41,7 +45,7 @@ def _run(rank, world, port, q):
         from synthefy_nori_b200 import ops
 
         ops.check_status(dev)
-        q.put((rank, part, ref))
+        q.put((rank, part, ref, part_q8))
     finally:
         dist.barrier()
         dist.destroy_process_group()
@@ -62,9 +66,10 @@ def test_sharded_context_matches_single_gpu_cache(world):
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    got = torch.cat([r[1] for r in res], 1)
     ref = res[0][2]
-    assert got.shape == ref.shape
-    cos = torch.nn.functional.cosine_similarity(got.flatten(), ref.flatten(), dim=0).item()
-    assert cos > 0.999, cos
-    assert (got - ref).abs().max().item() < 0.05 * ref.abs().max().item() + 0.02
+    for k in (1, 3):  # staged tcgen05 path, in-place multi-shard int8 kernel
+        got = torch.cat([r[k] for r in res], 1)
+        assert got.shape == ref.shape
+        cos = torch.nn.functional.cosine_similarity(got.flatten(), ref.flatten(), dim=0).item()
+        assert cos > 0.999, cos
+        assert (got - ref).abs().max().item() < 0.05 * ref.abs().max().item() + 0.02

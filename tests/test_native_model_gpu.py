@@ -17,6 +17,10 @@ def _config(name):
         from synthefy_nori_b200.models.config import _preset
 
         return _preset(embed_dim=88, hid_dim=96, nhead=2, nlayers=2)
+    if name == "logn-temp":  # log-n query scaling + learnable temperature, folded into the kernels
+        cfg = preset_config("nori-tiny")
+        cfg.update(use_logn_attention=True, use_learnable_attn_temperature=True, attn_n_ref=64.0)
+        return cfg
     return preset_config(name)
 
 
@@ -44,7 +48,7 @@ def _cos(a, b):
     return float((a @ b) / (a.norm() * b.norm() + 1e-30))
 
 
-@pytest.mark.parametrize("name", ["nori-tiny", "nori-6m", "padded", "nori-30m"])
+@pytest.mark.parametrize("name", ["nori-tiny", "nori-6m", "padded", "nori-30m", "logn-temp"])
 def test_native_forward_matches_fp32(name):
     m = _model(name).eval()
     x, y, ep = _data()
@@ -61,9 +65,13 @@ def test_native_forward_matches_fp32(name):
     assert _cos(auto, ref) > 0.999
 
 
-@pytest.mark.parametrize("name", ["nori-tiny", "padded"])
+@pytest.mark.parametrize("name", ["nori-tiny", "padded", "logn-temp"])
 def test_native_backward_matches_fp32(name):
     m = _model(name).train()
+    if name == "logn-temp":  # temperatures away from 1 (and one negative: |t| is used)
+        with torch.no_grad():
+            for i, (n, p) in enumerate((n, p) for n, p in m.named_parameters() if n.endswith("attn_temperature")):
+                p.fill_(1.3 if i % 2 else -0.8)
     x, y, ep = _data()
     q = torch.tensor(m.regression_quantiles, device="cuda")
     m.zero_grad()
