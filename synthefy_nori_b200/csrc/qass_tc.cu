@@ -43,16 +43,22 @@ constexpr int kThreads = 10 * 32;
 constexpr int kSRow = 68;   // fp32 stride of one head's base-scale row (spreads heads over banks)
 constexpr int kMaxHeads = 16;
 
-// barrier indices (per slot s: index + s)
+// barrier indices (per slot s: index + s); the forward's q tiles arrive through a ring of
+// kRing stages of their own (kRingFull / kRingEmpty + stage), so the loads run several
+// tiles ahead of the two compute slots
+constexpr int kRing = 6;
 enum : int { kLoad = 0, kMma1 = 2, kGReady = 4, kMma2 = 6, kDz2 = 8, kMma3 = 10, kDz1 = 12, kMma4 = 14,
-             kTFree = 16, kAcc = 18, kNumBars = 19 };
+             kTFree = 16, kAcc = 18, kRingFull = 19, kRingEmpty = kRingFull + kRing, kNumBars = kRingEmpty + kRing };
 
 template <bool BWD>
 struct Lay {
   static constexpr int kW1 = 0, kW2 = 8192, kOneHot = 16384, kOnes = 20480, kSlot0 = 24576;
   static constexpr int kQ = 0, kG = 16384, kDz2 = 32768, kDz1 = 49152, kDout = 65536;  // within a slot
+  // forward: the slots hold only their G tile; q tiles sit in the ring after them
   static constexpr int kSlotBytes = BWD ? 98304 : 32768;
-  static constexpr int kB1 = kSlot0 + 2 * kSlotBytes;
+  static constexpr int kRing0 = kSlot0 + 2 * kSlotBytes;
+  static constexpr int kRingBytes = BWD ? 0 : kRing * 16384;
+  static constexpr int kB1 = kRing0 + kRingBytes;
   static constexpr int kB2 = kB1 + 256;
   static constexpr int kS = kB2 + 256;
   static constexpr int kBar = kS + kMaxHeads * kSRow * 4;
@@ -185,6 +191,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar[kMma4 + s], 1);
       mbar_init(&bar[kTFree + s], 128);
     }
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(&bar[kRingFull + i], 1);
+      mbar_init(&bar[kRingEmpty + i], 128);  // the epilogue warpgroup that used the tile
+    }
     mbar_init(&bar[kAcc], 1);
     fence_barrier_init();
   }
@@ -197,7 +207,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
-    if (elect_one()) {
+    if (!BWD && elect_one()) {
+      for (int i = 0; i < my_tiles; ++i) {
+        const int st = i % kRing;
+        if (!mbar_wait(&bar[kRingEmpty + st], ((i / kRing) & 1) ^ 1, p.status, kTimeoutProducer, abort)) break;
+        const int64_t tile = blockIdx.x + static_cast<int64_t>(i) * gridDim.x;
+        const int r0 = static_cast<int>(tile * 128 / H);
+        mbar_arrive_expect_tx(&bar[kRingFull + st], 16384);
+        tma_load_3d(sm + L::kRing0 + st * 16384, &tmq, &bar[kRingFull + st], 0, 0, r0);
+      }
+      // never leave with copies in flight: wait (bounded, ignoring aborts) for the last ones
+      for (int i = my_tiles > kRing ? my_tiles - kRing : 0; i < my_tiles; ++i)
+        mbar_wait(&bar[kRingFull + i % kRing], static_cast<uint32_t>(i / kRing) & 1, nullptr, 0, nullptr);
+    } else if (BWD && elect_one()) {
       int issued[2] = {-1, -1};
       for (int i = 0; i < my_tiles; ++i) {
         const int s = i & 1;
@@ -242,11 +264,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t slot = sbase + L::kSlot0 + s * L::kSlotBytes;
           const uint32_t tA = tmem + s * 128, tB = tA + 64;
           if (state[s] == 0) {
-            if (!mbar_try_wait(&bar[kLoad + s], par)) continue;
+            const uint32_t qt = BWD ? slot + L::kQ : sbase + L::kRing0 + (i % kRing) * 16384;
+            if (BWD ? !mbar_try_wait(&bar[kLoad + s], par)
+                    : !mbar_try_wait(&bar[kRingFull + i % kRing], static_cast<uint32_t>(i / kRing) & 1))
+              continue;
             tc_fence_after();
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              umma_bf16_ss(tA, umma_desc_kmajor_sw128(slot + L::kQ + k * 32), umma_desc_kmajor_sw128(w1 + k * 32),
+              umma_bf16_ss(tA, umma_desc_kmajor_sw128(qt + k * 32), umma_desc_kmajor_sw128(w1 + k * 32),
                            id_kk, k > 0);
             umma_commit(&bar[kMma1 + s]);
             state[s] = 1;
@@ -374,7 +399,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&bar[kGReady + s]);
       // phase 2: z2 -> output (forward) or dz2, X and the direct part of dq (backward)
       if (!mbar_wait_warp(&bar[kMma2 + s], par, p.status, kTimeoutEpilogue, abort)) { ok = false; break; }
-      if (!mbar_wait_warp(&bar[kLoad + s], par, p.status, kTimeoutEpilogue, abort)) { ok = false; break; }
+      const uint32_t qtile = BWD ? slot + L::kQ : sbase + L::kRing0 + (i % kRing) * 16384;
+      if (BWD ? !mbar_wait_warp(&bar[kLoad + s], par, p.status, kTimeoutEpilogue, abort)
+              : !mbar_wait_warp(&bar[kRingFull + i % kRing], static_cast<uint32_t>(i / kRing) & 1, p.status,
+                                kTimeoutEpilogue, abort)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       float dqd[2][32];
 #pragma unroll
@@ -382,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t z[32];
         tmem_ld32(tB + 32 * c, z);
         uint32_t qw[16];
-        load_row32_bf16(slot + L::kQ, r, c, qw);
+        load_row32_bf16(qtile, r, c, qw);
         tmem_wait_ld();
         if (!BWD) {
           uint32_t ow[16];
@@ -431,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!BWD) {
         tc_fence_before();
-        mbar_arrive(&bar[kTFree + s]);
+        mbar_arrive(&bar[kRingEmpty + i % kRing]);  // the q tile's stage may be refilled
         continue;
       }
       fence_proxy_async_smem();

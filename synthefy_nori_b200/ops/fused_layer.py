@@ -32,6 +32,7 @@ kernel. Layers are wrapped in activation checkpointing by the caller.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -194,9 +195,9 @@ def _temperature_grad(info, n_keys: int, mult: float, dq: torch.Tensor, q: torch
     return (dmult * _logn(info, n_keys) * torch.sign(t.detach())).reshape(t.shape).to(t.dtype)
 
 
-# the feature-attention backward on the tcgen05 kernel (True) or the single-tile mma.sync
-# kernel (False, the faster of the two on the training shapes measured so far)
-FEAT_BWD_TC = False
+# the feature-attention backward on the tcgen05 kernel (True, the default) or the
+# single-tile mma.sync kernel (NORI_FEAT_BWD_TC=0)
+FEAT_BWD_TC = os.environ.get("NORI_FEAT_BWD_TC", "1") == "1"
 
 
 def _feat_attention_fwd(y: torch.Tensor, o: torch.Tensor, g: Geometry, lse: torch.Tensor | None = None,
