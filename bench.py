@@ -78,6 +78,9 @@ def parse():
                          "launcher enables it (dynamic), or eager (none); a compile failure falls back to eager "
                          "and is reported in the JSON line")
     ap.add_argument("--bucket-mb", type=float, default=25.0, help="peer DDP gradient bucket size (MB)")
+    ap.add_argument("--profile-kernels", type=int, default=0,
+                    help="after the timed region, profile one more (untimed) step on every rank and print "
+                         "rank 0's top-N kernels by device time to stderr")
     ap.add_argument("--shape-palette", type=int, default=4,
                     help="number of (rows, context rows) pairs drawn once from the shape distribution and cycled over "
                          "the steps (0: a fresh shape every step); warm-up steps cover the palette, so the "
@@ -207,6 +210,25 @@ def count_native_launches(step_fn) -> int:
     return n
 
 
+def _print_kernel_profile(step_fn, top: int, rank: int) -> None:
+    """One profiled step (every rank runs it: the step has collectives); rank 0 prints the
+    kernels with the most device time (all streams) to stderr."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    if rank != 0:
+        return
+    rows = sorted(((ev.self_device_time_total / 1000.0, ev.count, ev.key[:100]) for ev in prof.key_averages()
+                   if getattr(ev, "self_device_time_total", 0) > 0), reverse=True)
+    tot = sum(r[0] for r in rows)
+    print(f"[profile] kernels in one step: {tot:.1f} ms (summed over streams), {sum(r[1] for r in rows)} launches",
+          file=sys.stderr)
+    for ms, n, k in rows[:top]:
+        print(f"[profile] {ms:9.1f} ms {n:5d}  {k}", file=sys.stderr)
+
+
 # ----------------------------------------------------------------------------- arms
 def run_ours(args, device, world, rank):
     from synthefy_nori_b200 import ops
@@ -240,6 +262,8 @@ def run_ours(args, device, world, rank):
     launches = count_native_launches(lambda: one(args.warmup + args.steps)) * args.steps
     ops.check_status(device)
     e2e = None if args.no_e2e else run_e2e(args, trainer, shapes, device, world, rank)
+    if args.profile_kernels > 0:
+        _print_kernel_profile(lambda: one(args.warmup + args.steps), args.profile_kernels, rank)
     info = {}
     if trainer.peer is not None:
         info["grad_buckets"] = trainer.peer.describe()

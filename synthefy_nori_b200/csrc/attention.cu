@@ -21,6 +21,7 @@
 #include <torch/extension.h>
 
 #include "sm100.cuh"
+#include "tma_host.h"
 
 namespace nori {
 
@@ -914,7 +915,7 @@ void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
       small_smem_set[dev] = 1;
     }
     const int sms = at::cuda::getDeviceProperties(dev)->multiProcessorCount;
-    const int64_t grid = std::min<int64_t>(BH, static_cast<int64_t>(sms) * kSmallCtasPerSm);
+    const int64_t grid = std::min<int64_t>(BH, static_cast<int64_t>(persistent_sms(sms)) * kSmallCtasPerSm);
     attn_bwd_small_kernel<<<static_cast<unsigned>(grid), kAttnThreads, kSmallSmem, stream>>>(p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return;

@@ -1035,7 +1035,7 @@ void attn_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
   static int n_sm[64] = {0};
   if (n_sm[dev] == 0) C10_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev));
   // persistent: one CTA per SM, each looping over work items
-  dim3 grid(static_cast<unsigned>(std::min<int64_t>(p.n_items, n_sm[dev])));
+  dim3 grid(static_cast<unsigned>(std::min<int64_t>(p.n_items, persistent_sms(n_sm[dev]))));
   attn_fwd_tc_kernel<<<grid, fa::kThreads, fa::kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(mq.map, mk.map, mv.map, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -1104,7 +1104,7 @@ void attn_bwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
   static int n_sm[64] = {0};
   if (n_sm[dev] == 0) C10_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev));
   // persistent: one CTA per SM, each looping over (head, key tile) work items
-  attn_bwd_tc_kernel<<<static_cast<unsigned>(std::min<int64_t>(p.n_items, n_sm[dev])), fb::kThreads, fb::kSmemBytes,
+  attn_bwd_tc_kernel<<<static_cast<unsigned>(std::min<int64_t>(p.n_items, persistent_sms(n_sm[dev]))), fb::kThreads, fb::kSmemBytes,
                        at::cuda::getCurrentCUDAStream()>>>(mq.map, mk.map, mv.map, mdo.map, mdq.map, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

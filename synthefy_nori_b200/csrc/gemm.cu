@@ -20,8 +20,9 @@
 //               stores of 128 x 32 boxes (tails clipped by the tensor map).
 //
 // Epilogues (ops the Nori encoder layer fuses into its GEMMs):
-//   kStore    out = bf16(acc * row_scale[m] + bias[n])   (RMSNorm without affine weight
-//             commutes with the GEMM: rms(x) W^T = diag(r) x W^T)
+//   kStore    out = bf16(act(acc * row_scale[m] + bias[n]))   (RMSNorm without affine
+//             weight commutes with the GEMM: rms(x) W^T = diag(r) x W^T; act = identity or
+//             the exact GELU of a GELU MLP's first projection)
 //   kSwiGLU   weight rows interleaved (gate_j, up_j): out[m, j] = silu(g r) * (u r)
 //   kResidual out = bf16(resid[m, n] + alpha * acc) (resid tile TMA-loaded into the
 //             staging buffer), with each row's sum of squares added to sumsq[m]
@@ -32,6 +33,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
+
+#include <atomic>
 
 #include "sm100.cuh"
 #include "tma_host.h"
@@ -49,6 +52,7 @@ struct GemmParams {
   const float* bias;       // [N] or null
   float alpha;
   float* sumsq;  // [M] or null
+  int act;       // kStore: 0 none, 1 exact GELU applied after scale and bias
   int* status;
 };
 
@@ -284,6 +288,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               if (col < p.N) v[i] += p.bias[col];
             }
           }
+          if (p.act == 1) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0.5f * v[i] * (1.0f + erff(v[i] * 0.70710678118654752f));
+          }
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
             uint4 w = make_uint4(pack_bf16x2(v[8 * cc], v[8 * cc + 1]), pack_bf16x2(v[8 * cc + 2], v[8 * cc + 3]),
@@ -368,6 +376,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
+static std::atomic<int> g_sm_reserve{0};
+int sm_reserve() { return g_sm_reserve.load(std::memory_order_relaxed); }
+void set_sm_reserve(int64_t n) {
+  TORCH_CHECK(n >= 0 && n < 64, "sm_reserve must be in [0, 64)");
+  g_sm_reserve.store(static_cast<int>(n), std::memory_order_relaxed);
+}
+
 static int num_sms(int dev) {
   static int cache[64] = {0};
   if (cache[dev] == 0) cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev);
@@ -409,7 +424,7 @@ static void launch_gemm(const Operand& A, const Operand& B, const torch::Tensor*
     configured[dev] = true;
   }
   const int items = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * p.k_splits;
-  const int grid = std::max(1, std::min(items, num_sms(dev)));
+  const int grid = std::max(1, std::min(items, persistent_sms(num_sms(dev))));
   kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, tr, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -467,10 +482,10 @@ static const float* opt_f32(const c10::optional<torch::Tensor>& t, int64_t n, co
   return t->data_ptr<float>();
 }
 
-// out = bf16((A @ W^T) * row_scale[:, None] + bias).  A [M, K]; W [N, K] (or w_kn: W stored [K, N]).
+// out = bf16(act((A @ W^T) * row_scale[:, None] + bias)).  A [M, K]; W [N, K] (or w_kn: W stored [K, N]).
 torch::Tensor gemm_bf16(const torch::Tensor& A, const torch::Tensor& W, const c10::optional<torch::Tensor>& row_scale,
                         const c10::optional<torch::Tensor>& bias, const torch::Tensor& status, int64_t bn, bool w_kn,
-                        double alpha, const c10::optional<torch::Tensor>& out_opt) {
+                        double alpha, const c10::optional<torch::Tensor>& out_opt, int64_t act) {
   check_operand(A, "A");
   check_operand(W, "W");
   const int64_t N = w_kn ? W.size(1) : W.size(0);
@@ -486,6 +501,8 @@ torch::Tensor gemm_bf16(const torch::Tensor& A, const torch::Tensor& W, const c1
   p.row_scale = opt_f32(row_scale, p.M, "row_scale");
   p.bias = opt_f32(bias, p.N, "bias");
   p.alpha = static_cast<float>(alpha);
+  TORCH_CHECK(act == 0 || act == 1, "gemm: act must be 0 (none) or 1 (gelu)");
+  p.act = static_cast<int>(act);
   const int b = bn > 0 ? static_cast<int>(bn) : choose_bn(p.N);
   Operand oa{&A, false}, ow{&W, w_kn};
   auto s = at::cuda::getCurrentCUDAStream();

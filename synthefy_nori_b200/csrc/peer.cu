@@ -42,6 +42,7 @@
 #include <torch/extension.h>
 
 #include "sm100.cuh"
+#include "tma_host.h"
 
 namespace nori {
 
@@ -339,8 +340,9 @@ void peer_bucket_pack_signal(int64_t grad, int64_t wire, int64_t b0, int64_t n, 
   TORCH_CHECK(b0 % 4 == 0 && n % 4 == 0 && n >= 0, "bucket bounds must be multiples of 4 elements");
   PeerSet ps = make_set(flags.size(), {}, {}, flags, {});
   const int W = static_cast<int>(flags.size());
-  const int blocks = wire != 0 ? static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n / 4 + 255) / 256,
-                                                                                          2 * sm_count(device))))
+  // with SMs reserved for the communication kernels, the pack stays within them
+  const int cap = sm_reserve() > 0 ? 2 * sm_reserve() : 2 * sm_count(device);
+  const int blocks = wire != 0 ? static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n / 4 + 255) / 256, cap)))
                                : 1;
   bucket_pack_signal_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const float*>(grad), reinterpret_cast<__nv_bfloat16*>(wire), b0, n,

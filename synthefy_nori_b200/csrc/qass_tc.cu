@@ -607,7 +607,7 @@ void qass_tc_launch(bool bwd, const torch::Tensor& q, const torch::Tensor* dout,
       C10_CUDA_CHECK(cudaFuncSetAttribute(qtc::qass_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       set_b[dev] = 1;
     }
-    const int grid = static_cast<int>(std::min<int64_t>(tiles, qtc_sms(dev)));
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, persistent_sms(qtc_sms(dev))));
     qtc::qass_tc_kernel<true><<<grid, qtc::kThreads, smem, stream>>>(tmq, tmdo, p);
   } else {
     constexpr int smem = qtc::Lay<false>::kAlloc;
@@ -615,7 +615,7 @@ void qass_tc_launch(bool bwd, const torch::Tensor& q, const torch::Tensor* dout,
       C10_CUDA_CHECK(cudaFuncSetAttribute(qtc::qass_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       set_f[dev] = 1;
     }
-    const int grid = static_cast<int>(std::min<int64_t>(tiles, qtc_sms(dev)));
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, persistent_sms(qtc_sms(dev))));
     qtc::qass_tc_kernel<false><<<grid, qtc::kThreads, smem, stream>>>(tmq, tmdo, p);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();

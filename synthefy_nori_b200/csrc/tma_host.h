@@ -120,4 +120,13 @@ inline Map5 make_map(const torch::Tensor& t, const std::vector<int64_t>& l, int6
   return m;
 }
 
+// SMs kept free of the persistent (one CTA per SM) kernels while gradient-communication
+// kernels run beside them on other streams: a persistent grid that covers every SM would
+// otherwise have a CTA waiting for an SM held by a communication kernel (which may itself
+// be waiting for a peer), stretching the whole kernel. Set by the multi-GPU data-parallel
+// path; 0 (every SM) otherwise.
+int sm_reserve();
+void set_sm_reserve(int64_t n);
+inline int persistent_sms(int n_sm) { return std::max(1, n_sm - sm_reserve()); }
+
 }  // namespace nori

@@ -26,6 +26,7 @@ __all__ = [
     "rms_apply",
     "rms_bwd",
     "swiglu_bwd",
+    "gelu_bwd",
     "sumsq_to_scale",
     "pinball_loss_grad",
     "grad_sumsq",
@@ -66,12 +67,16 @@ def check_status(device: torch.device) -> None:
 
 
 def gemm(a: torch.Tensor, w: torch.Tensor, row_scale=None, bias=None, bn: int = 0, w_kn: bool = False,
-         alpha: float = 1.0, out=None) -> torch.Tensor:
-    """bf16 ``(a @ W.T) * row_scale[:, None] + bias`` on tcgen05 (fp32 accumulation).
+         alpha: float = 1.0, out=None, act: str | None = None) -> torch.Tensor:
+    """bf16 ``act((a @ W.T) * row_scale[:, None] + bias)`` on tcgen05 (fp32 accumulation);
+    ``act`` is None or ``"gelu"`` (exact, erf form).
 
     ``w`` is ``W`` [N, K], or with ``w_kn=True`` the same matrix stored as [K, N]
     (so ``gemm(dy, W, w_kn=True)`` is the input gradient ``dy @ W``)."""
-    return _lib().gemm_bf16(a, w, row_scale, bias, status_word(a.device), bn, w_kn, float(alpha), out)
+    if act not in (None, "gelu"):
+        raise ValueError(f"unsupported GEMM activation {act!r}")
+    return _lib().gemm_bf16(a, w, row_scale, bias, status_word(a.device), bn, w_kn, float(alpha), out,
+                            1 if act == "gelu" else 0)
 
 
 def gemm_swiglu(a: torch.Tensor, w_interleaved: torch.Tensor, row_scale=None, bn: int = 0) -> torch.Tensor:
@@ -177,6 +182,11 @@ def rms_scale(x: torch.Tensor, eps: float) -> torch.Tensor:
 
 def rms_apply(x: torch.Tensor, rs: torch.Tensor) -> torch.Tensor:
     return _lib().rms_apply(x, rs)
+
+
+def gelu_bwd(dh: torch.Tensor, z: torch.Tensor) -> torch.Tensor:
+    """``dh * GELU'(z)`` (exact GELU) for the bf16 pre-activation ``z``."""
+    return _lib().gelu_bwd(dh.contiguous(), z.contiguous())
 
 
 def swiglu_bwd(dh: torch.Tensor, gu: torch.Tensor) -> torch.Tensor:

@@ -96,7 +96,8 @@ def exchange_handles(local: dict, group=None) -> list[dict]:
 class PeerDDP:
     def __init__(self, model, device: torch.device, group=None, lr=3e-4, betas=(0.9, 0.95), eps=1e-8,
                  weight_decay=0.01, ema_decay=0.999, max_grad_norm=1.0, bucket_mb: float = 25.0,
-                 wire: str = "bf16", wait_limit_s: float = 60.0, align: int = 64, record_timeline: bool = False):
+                 wire: str = "bf16", wait_limit_s: float = 60.0, align: int = 64, record_timeline: bool = False,
+                 sm_reserve: int = 4):
         from synthefy_nori_b200 import ops
         from synthefy_nori_b200.ops.weight_layouts import WeightLayouts
 
@@ -112,6 +113,13 @@ class PeerDDP:
         self.device = device
         self.wire_bf16 = wire == "bf16"
         self.wait_limit_s = float(wait_limit_s)
+        # the bucket kernels (flag wait, pack, reduce) run on side streams during the
+        # backward; the persistent compute kernels leave `sm_reserve` SMs to them, so neither
+        # side waits for an SM the other holds (a flag wait can last until the peer catches up)
+        self.sm_reserve = int(sm_reserve) if self.world > 1 else 0
+        self._prev_reserve = C.sm_reserve()
+        C.set_sm_reserve(max(self._prev_reserve, self.sm_reserve))
+        self.reduce_ctas = 2 * self.sm_reserve if self.sm_reserve > 0 else 64
         self.params = [p for p in model.parameters() if p.requires_grad]
         order = list(reversed(self.params))  # the backward pass produces gradients roughly in this order
         offs, self.numel, self.buckets = plan_buckets([p.numel() for p in order], int(bucket_mb * 2 ** 20 / 4),
@@ -297,7 +305,8 @@ class PeerDDP:
             self.C.peer_wait(self.ptrs["flags"][rank], b * W, W, self.flag_step, self.wait_limit_s, st)
             roff, f0, n = self.pieces[b]
             self.C.peer_bucket_reduce(self.ptrs["wire"], f0, n, self.wire_bf16, 1.0 / W,
-                                      self.red.data_ptr() + 4 * roff, self.norm_acc.data_ptr(), st, 64)
+                                      self.red.data_ptr() + 4 * roff, self.norm_acc.data_ptr(), st,
+                                      self.reduce_ctas)
             if self.record_timeline:
                 ev1 = torch.cuda.Event(enable_timing=True)
                 ev1.record(self.comm)
@@ -394,6 +403,8 @@ class PeerDDP:
         for h in self._hooks:
             h.remove()
         self._hooks = []
+        if self.C.sm_reserve() == max(self._prev_reserve, self.sm_reserve):
+            self.C.set_sm_reserve(self._prev_reserve)
         ref = getattr(self._model, "_nori_layout_owner", None)
         if ref is not None and ref() is self:
             del self._model._nori_layout_owner

@@ -80,3 +80,20 @@ def test_gemm_wgrad(T, No, Ki):
     ref = out + dy.float().T @ x.float()
     ops.gemm_wgrad(dy, x, out)
     torch.testing.assert_close(out, ref, atol=5e-2, rtol=1e-2)
+
+
+def test_gemm_gelu_epilogue_and_backward():
+    """Exact GELU in the store epilogue (after the row scale) and the GELU backward kernel,
+    against fp32 PyTorch."""
+    torch.manual_seed(4)
+    a = torch.randn(300, 192, device="cuda").to(torch.bfloat16)
+    w = (0.1 * torch.randn(136, 192, device="cuda")).to(torch.bfloat16)
+    rs = torch.rand(300, device="cuda") + 0.5
+    z = (a.float() @ w.float().t()) * rs[:, None]
+    out = ops.gemm(a, w, row_scale=rs, act="gelu")
+    torch.testing.assert_close(out.float(), torch.nn.functional.gelu(z), atol=2e-2, rtol=2e-2)
+    zb = z.to(torch.bfloat16)
+    dh = torch.randn_like(zb)
+    zf = zb.float().requires_grad_(True)
+    torch.nn.functional.gelu(zf).backward(dh.float())
+    torch.testing.assert_close(ops.gelu_bwd(dh, zb).float(), zf.grad, atol=2e-2, rtol=2e-2)
