@@ -34,6 +34,8 @@ void attn_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Te
 bool attn_feat_tc_supported(int64_t T, int64_t d_valid);
 int sm_reserve();
 void set_sm_reserve(int64_t n);
+void head_rmsnorm_(torch::Tensor& x, int64_t heads, int64_t D, const c10::optional<torch::Tensor>& gain, double eps,
+                   double post);
 void attn_feat_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
                       const c10::optional<torch::Tensor>& lse, std::vector<int64_t> lq, std::vector<int64_t> lk,
                       std::vector<int64_t> lv, std::vector<int64_t> lo, int64_t BH, int64_t T, int64_t d_valid,
@@ -161,6 +163,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_feat_tc_supported", &nori::attn_feat_tc_supported);
   m.def("sm_reserve", &nori::sm_reserve);
   m.def("set_sm_reserve", &nori::set_sm_reserve);
+  m.def("head_rmsnorm_", &nori::head_rmsnorm_);
   m.def("attn_feat_fwd_tc", &nori::attn_feat_fwd_tc);
   m.def("attn_feat_bwd_tc", &nori::attn_feat_bwd_tc);
   m.def("attn_bwd_tc", &nori::attn_bwd_tc);

@@ -272,6 +272,25 @@ class FeaturesTransformer(nn.Module):
         return result
 
     # ------------------------------------------------------------------ dispatch
+    def use_native_two_phase(self, device: torch.device) -> bool:
+        """The two-phase encoder runs on the native kernels for inference (no autograd) on
+        CUDA when its dimensions fit them; training and other shapes use the module."""
+        if self.two_phase_config is None or self.impl == "torch" or device.type != "cuda" or torch.is_grad_enabled():
+            return False
+        from synthefy_nori_b200 import ops
+
+        if not ops.native_available():
+            raise RuntimeError(
+                "synthefy_nori_b200 native extension is not built; run `python setup.py build_ext --inplace` "
+                f"(import error: {ops.native_import_error()})"
+            )
+        from synthefy_nori_b200.ops import two_phase as native_two_phase
+
+        ok = native_two_phase.supported(self.transformer_encoder)
+        if not ok and self.impl == "native":
+            raise NotImplementedError("impl='native': the native kernels do not cover this two-phase encoder")
+        return ok
+
     def use_native(self, device: torch.device) -> bool:
         if self.impl == "torch":
             return False
@@ -412,7 +431,13 @@ class FeaturesTransformer(nn.Module):
             raise ValueError("the two-phase encoder supports regression only; pass task_type='reg'")
         xe, ye, pre, pad, masked_y = self.embed(x, y, eval_pos, task_type)
         if self.two_phase_config is not None:
-            rows, cells = self.transformer_encoder(xe, masked_y, eval_pos)
+            if self.use_native_two_phase(xe.device):
+                from synthefy_nori_b200.ops import two_phase as native_two_phase
+
+                rows, cells = native_two_phase.forward(self.transformer_encoder, xe, masked_y, eval_pos)
+                rows, cells = rows.to(xe.dtype), cells.to(xe.dtype)
+            else:
+                rows, cells = self.transformer_encoder(xe, masked_y, eval_pos)
             if return_embeddings:
                 return rows
             reg = self.reg_y_decoder(rows[:, eval_pos:])

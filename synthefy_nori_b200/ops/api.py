@@ -24,6 +24,7 @@ __all__ = [
     "feat_tc_supported",
     "rms_scale",
     "rms_apply",
+    "head_rmsnorm_",
     "rms_bwd",
     "swiglu_bwd",
     "gelu_bwd",
@@ -182,6 +183,13 @@ def rms_scale(x: torch.Tensor, eps: float) -> torch.Tensor:
 
 def rms_apply(x: torch.Tensor, rs: torch.Tensor) -> torch.Tensor:
     return _lib().rms_apply(x, rs)
+
+
+def head_rmsnorm_(x: torch.Tensor, heads: int, d: int, gain=None, eps: float = 1e-6, post: float = 1.0) -> torch.Tensor:
+    """In place: every ``d``-wide head block of the bf16 rows of ``x`` becomes
+    ``block * rsqrt(mean(block**2) + eps) * gain * post`` (fp32 math; ``gain`` fp32 ``[d]``)."""
+    _lib().head_rmsnorm_(x, int(heads), int(d), gain, float(eps), float(post))
+    return x
 
 
 def gelu_bwd(dh: torch.Tensor, z: torch.Tensor) -> torch.Tensor:
