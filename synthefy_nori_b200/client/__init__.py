@@ -6,8 +6,10 @@ framework.  ``mode="remote"`` POSTs the hosted API's JSON contract (see
 <scheme> <api_key>``; responses 408 / 409 / 425 / 429 / 5xx and connection errors are
 retried up to ``max_retries`` times, waiting ``Retry-After`` seconds when the server sends
 it, else ``min(2^attempt, 30) * U[0.5, 1]`` seconds.  NaN features travel as ``null``;
-non-finite targets are rejected before sending.  ``mode="sagemaker"`` needs ``boto3`` and
-AWS credentials (S3-staged asynchronous inference) and raises when ``boto3`` is absent.
+non-finite targets are rejected before sending.  ``mode="sagemaker"`` runs S3-staged
+asynchronous invocations of a SageMaker endpoint (``client.sagemaker``): its AWS clients
+come from ``boto3`` (standard credential chain) or are passed in as
+``sagemaker_runtime_client=`` / ``s3_client=``.
 """
 
 from __future__ import annotations
@@ -52,7 +54,8 @@ class SynthefyNoriClient:
                  model_path: str | None = None, weights: str | None = None, device=None, base_url: str | None = None,
                  endpoint: str = DEFAULT_ENDPOINT, timeout: float = 300.0, max_retries: int = 2,
                  auth_scheme: str = "Bearer", endpoint_name: str | None = None, region_name: str | None = None,
-                 s3_staging_uri: str | None = None, **regressor_kwargs):
+                 s3_staging_uri: str | None = None, sagemaker_runtime_client=None, s3_client=None,
+                 **regressor_kwargs):
         if mode not in ("local", "remote", "sagemaker"):
             raise ValueError(f"mode must be 'local', 'remote' or 'sagemaker'; got {mode!r}")
         if model is None and model_path is None:
@@ -73,13 +76,13 @@ class SynthefyNoriClient:
             self.endpoint, self.auth_scheme = endpoint, auth_scheme
             self.http = httpx.Client(base_url=self.base_url)
         else:
-            try:
-                import boto3  # noqa: F401
-            except ImportError as exc:
-                raise RuntimeError("mode='sagemaker' needs boto3 and AWS credentials") from exc
+            from synthefy_nori_b200.client.sagemaker import SageMakerTransport
+
             if not endpoint_name or not s3_staging_uri:
                 raise ValueError("mode='sagemaker' needs endpoint_name= and s3_staging_uri=")
-            raise NotImplementedError("SageMaker asynchronous inference is not provided by this build")
+            self.endpoint_name = endpoint_name
+            self.sagemaker = SageMakerTransport(endpoint_name, s3_staging_uri, runtime_client=sagemaker_runtime_client,
+                                                s3_client=s3_client, region_name=region_name, timeout=timeout)
 
     def __enter__(self):
         return self
@@ -96,6 +99,11 @@ class SynthefyNoriClient:
     def predict(self, X_train, y_train, X_test, *, output_type: str = "mean", quantiles=None, discretize=None,
                 categorical_levels=None, memory_policy=None, large_context_policy=None,
                 large_context_threshold=None):
+        if self.mode == "sagemaker":
+            return self._predict_sagemaker(X_train, y_train, X_test, output_type=output_type, quantiles=quantiles,
+                                           discretize=discretize, categorical_levels=categorical_levels,
+                                           memory_policy=memory_policy, large_context_policy=large_context_policy,
+                                           large_context_threshold=large_context_threshold)
         if self.mode == "remote":
             return self._predict_remote(X_train, y_train, X_test, output_type=output_type, quantiles=quantiles,
                                         discretize=discretize, categorical_levels=categorical_levels,
@@ -168,7 +176,35 @@ class SynthefyNoriClient:
         raise APIConnectionError("request failed after retries")
 
     def _predict_remote(self, X_train, y_train, X_test, **opt):
-        data = self._post(self._payload(X_train, y_train, X_test, **opt))
+        return self._parse(self._post(self._payload(X_train, y_train, X_test, **opt)), opt)
+
+    # ------------------------------------------------------------------ SageMaker
+    def _predict_sagemaker(self, X_train, y_train, X_test, **opt):
+        """One S3-staged asynchronous invocation of the endpoint (``client.sagemaker``): the
+        arrays travel in a request tensor file, the options in its metadata."""
+        y = np.asarray(y_train, np.float64)
+        if not np.all(np.isfinite(y)):
+            raise ValueError("y_train must contain only finite numbers for hosted inference")
+
+        def mat(a):
+            a = np.asarray(a.to_numpy() if hasattr(a, "to_numpy") else a, np.float32)
+            return a[:, None] if a.ndim == 1 else a
+
+        meta = {"task": "regression"}
+        if opt.get("output_type") not in (None, "mean"):
+            meta["output_type"] = opt["output_type"]
+        for k in ("quantiles", "discretize", "categorical_levels", "memory_policy", "large_context_policy",
+                  "large_context_threshold"):
+            if opt.get(k) is not None:
+                v = opt[k]
+                v = v.model_dump(exclude_unset=True) if hasattr(v, "model_dump") else v
+                meta[k] = v.tolist() if isinstance(v, np.ndarray) else v
+        data = self.sagemaker.invoke({"X_train": mat(X_train), "y_train": y, "X_test": mat(X_test)}, meta,
+                                     model=self.model)
+        return self._parse(data, opt)
+
+    @staticmethod
+    def _parse(data: dict, opt: dict):
         ot = opt.get("output_type") or "mean"
         if ot == "full":
             return {"quantiles": np.asarray(data["quantiles"], float), "taus": np.asarray(data["taus"], float),
@@ -178,4 +214,6 @@ class SynthefyNoriClient:
         return np.array([np.nan if v is None else v for v in data["predictions"]], float)
 
 
-__all__ = ["SynthefyNoriClient", "APIError", "APIConnectionError", "APITimeoutError"]
+from synthefy_nori_b200.client.sagemaker import SageMakerInvocationError  # noqa: E402
+
+__all__ = ["SynthefyNoriClient", "APIError", "APIConnectionError", "APITimeoutError", "SageMakerInvocationError"]

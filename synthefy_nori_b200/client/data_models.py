@@ -65,13 +65,11 @@ class MultiTargetPredictionPolicy(BaseModel):
     seed: int = Field(0, ge=0)
 
 
-class NoriPredictRequest(BaseModel):
-    """One prediction request: context ``X_train`` / ``y_train``, query ``X_test``."""
+class NoriPredictOptions(BaseModel):
+    """Everything of a prediction request except its arrays (the metadata of a request
+    tensor file carries exactly these fields)."""
 
     model_config = ConfigDict(extra="forbid")
-    X_train: list[list[Optional[float]]]
-    y_train: Union[list[float], list[list[float]]]
-    X_test: list[list[Optional[float]]]
     task: str = "regression"
     model: Optional[str] = None
     output_type: Optional[str] = None
@@ -105,6 +103,14 @@ class NoriPredictRequest(BaseModel):
         if v is not None and any(not 0.0 < q < 1.0 for q in v):
             raise ValueError("quantiles must lie in (0, 1)")
         return v
+
+
+class NoriPredictRequest(NoriPredictOptions):
+    """One prediction request: context ``X_train`` / ``y_train``, query ``X_test``."""
+
+    X_train: list[list[Optional[float]]]
+    y_train: Union[list[float], list[list[float]]]
+    X_test: list[list[Optional[float]]]
 
     @model_validator(mode="after")
     def _shapes(self):

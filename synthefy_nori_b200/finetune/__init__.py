@@ -18,8 +18,9 @@
   weights are written to ``output_path/<model_name>.pt`` in the release checkpoint
   format.  ``deploy`` starts this build's HTTP server (``serving.py``) with the
   fine-tuned model registered under its name;
-* ``backend="sagemaker"``: the reference's hosted Algorithm flow; it needs ``boto3`` and
-  AWS credentials and raises ``ImportError`` when ``boto3`` is absent.
+* ``backend="sagemaker"``: hosted jobs run by the Nori Algorithm and asynchronous
+  SageMaker endpoints (``finetune.sagemaker``); its AWS clients come from ``boto3`` or are
+  passed in (``sagemaker_client=``, ``s3_client=``, ``logs_client=``).
 """
 
 from __future__ import annotations
@@ -234,7 +235,8 @@ class _LocalJob:
 class SynthefyNoriFineTuner:
     """Fine-tuning jobs and the endpoints serving their results."""
 
-    def __init__(self, *, backend: str = "local", device=None, region_name: str | None = None):
+    def __init__(self, *, backend: str = "local", device=None, region_name: str | None = None,
+                 sagemaker_client=None, s3_client=None, logs_client=None, poll_s: float = 15.0):
         if backend not in ("local", "sagemaker"):
             raise ValueError("backend must be 'local' or 'sagemaker'")
         self.backend = backend
@@ -242,13 +244,12 @@ class SynthefyNoriFineTuner:
         self.region_name = region_name
         self._jobs: dict[str, _LocalJob] = {}
         self._servers: dict[str, tuple] = {}
+        self._sm = None
         if backend == "sagemaker":
-            try:
-                import boto3  # noqa: F401
-            except ImportError as exc:
-                raise ImportError("the sagemaker backend needs boto3 and AWS credentials; use backend='local' to "
-                                  "fine-tune on this machine's GPUs") from exc
-            raise NotImplementedError("the SageMaker Algorithm flow is not wired in this build; use backend='local'")
+            from synthefy_nori_b200.finetune.sagemaker import SageMakerJobs
+
+            self._sm = SageMakerJobs(region_name=region_name, sagemaker_client=sagemaker_client, s3_client=s3_client,
+                                     logs_client=logs_client, poll_s=poll_s)
 
     def __enter__(self):
         return self
@@ -273,6 +274,8 @@ class SynthefyNoriFineTuner:
                             steps_per_model=hp.n_steps_per_model, context_rows=n_ctx, query_rows=n_q)
 
     def fine_tune(self, request: FineTuneJobRequest, *, overwrite: bool = False) -> FineTuneJob:
+        if self._sm is not None:
+            return self._sm.fine_tune(request)
         out = os.path.join(request.output_path, f"{request.hyperparameters.model_name}.pt")
         if os.path.exists(out) and not overwrite:
             raise FineTuningError(f"{out} exists; pass overwrite=True to replace it")
@@ -287,9 +290,13 @@ class SynthefyNoriFineTuner:
         return self._jobs[job_name]
 
     def get_status(self, job_name: str) -> FineTuneJob:
+        if self._sm is not None:
+            return self._sm.get_status(job_name)
         return self._get(job_name).job
 
     def wait(self, job_name: str, *, poll_s: float = 1.0, timeout_s: float | None = None) -> FineTuneJob:
+        if self._sm is not None:
+            return self._sm.wait(job_name, poll_s=poll_s, timeout_s=timeout_s)
         j = self._get(job_name)
         j.thread.join(timeout_s)
         if j.thread.is_alive():
@@ -297,6 +304,8 @@ class SynthefyNoriFineTuner:
         return j.job
 
     def stop(self, job_name: str) -> FineTuneJob:
+        if self._sm is not None:
+            return self._sm.stop(job_name)
         j = self._get(job_name)
         j._stop.set()
         if j.job.status == "InProgress":
@@ -304,6 +313,9 @@ class SynthefyNoriFineTuner:
         return j.job
 
     def get_logs(self, job_name: str, *, follow: bool = False, poll_s: float = 0.5):
+        if self._sm is not None:
+            yield from self._sm.get_logs(job_name, follow=follow, poll_s=poll_s)
+            return
         j = self._get(job_name)
         i = 0
         while True:
@@ -318,14 +330,20 @@ class SynthefyNoriFineTuner:
             time.sleep(poll_s)
 
     def get_training_curves(self, job_name: str) -> dict:
-        r = self._get(job_name).report
+        r = self.get_training_report(job_name)
         return {f"model_{c.model_index}": c.model_dump() for c in r.curves}
 
     def get_training_report(self, job_name: str) -> TrainingReport:
+        if self._sm is not None:
+            return self._sm.get_training_report(job_name)
         return self._get(job_name).report
 
     # ---------------------------------------------------------------- serving
-    def deploy(self, job: FineTuneJob | str, *, host: str = "127.0.0.1", port: int = 0) -> FineTunedEndpoint:
+    def deploy(self, job: FineTuneJob | str, *, host: str = "127.0.0.1", port: int = 0, **sagemaker_kw) -> FineTunedEndpoint:
+        """Serve a completed job's model: this build's HTTP server (local backend) or an
+        asynchronous SageMaker endpoint (``endpoint_name=``, ``instance_type=``; sagemaker)."""
+        if self._sm is not None:
+            return self._sm.deploy(job if isinstance(job, str) else job.job_name, **sagemaker_kw)
         j = self._get(job if isinstance(job, str) else job.job_name)
         if j.job.status != "Completed" or not j.job.model_artifact:
             raise FineTuningError(f"job {j.name} has no completed model to deploy (status {j.job.status})")
@@ -355,6 +373,9 @@ class SynthefyNoriFineTuner:
 
     def undeploy(self, endpoint: FineTunedEndpoint | str, *, timeout_s: float = 30.0) -> None:
         name = endpoint if isinstance(endpoint, str) else endpoint.endpoint_name
+        if self._sm is not None:
+            self._sm.undeploy(name)
+            return
         srv = self._servers.pop(name, None)
         if srv is None:
             return
@@ -365,5 +386,14 @@ class SynthefyNoriFineTuner:
     def create_client(self, endpoint: FineTunedEndpoint, **kw):
         from synthefy_nori_b200.client import SynthefyNoriClient
 
+        if endpoint.backend == "sagemaker":
+            if self._sm is None:
+                raise FineTuningError("a SageMaker endpoint needs a tuner with backend='sagemaker'")
+            staging = kw.pop("s3_staging_uri", None) or self._sm.staging_uri(endpoint.endpoint_name)
+            if staging is None:
+                raise FineTuningError("pass s3_staging_uri= for an endpoint this tuner did not deploy")
+            return SynthefyNoriClient(mode="sagemaker", model=endpoint.model_name,
+                                      endpoint_name=endpoint.endpoint_name, s3_staging_uri=staging,
+                                      s3_client=kw.pop("s3_client", self._sm.s3), region_name=self.region_name, **kw)
         return SynthefyNoriClient(api_key=kw.pop("api_key", "local"), mode="remote", model=endpoint.model_name,
                                   base_url=endpoint.url, **kw)
