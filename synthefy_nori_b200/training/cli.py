@@ -116,7 +116,99 @@ def parse_args(argv=None):
     g.add_argument("--wandb-project", default=None)
     g.add_argument("--wandb-name", default=None)
     g.add_argument("--seed", type=int, default=0)
-    return ap.parse_args(argv)
+    _add_reference_flags(ap)
+    args = ap.parse_args(argv)
+    args.notices = _apply_reference_flags(args)
+    return args
+
+
+def _quantile_list(text: str) -> list:
+    qs = [float(v) for v in text.split(",") if v.strip()]
+    if not qs or any(not 0.0 < q < 1.0 for q in qs):
+        raise argparse.ArgumentTypeError("quantiles must be a comma-separated list in (0, 1)")
+    return qs
+
+
+def _add_reference_flags(ap) -> None:
+    """The reference launcher's flag names (``training/cli.py:424-1092`` of the reference),
+    so its launch scripts' command lines run here. Each maps onto a setting of this CLI or of
+    the model config; flags for machinery this build replaces (torch.compile, PyTorch's
+    RMSNorm / foreach EMA, autocast) are accepted and reported as not applying."""
+    g = ap.add_argument_group("reference launcher flags (mapped onto the settings above)")
+    g.add_argument("--regression-loss", default=None, choices=["mse", "smooth_l1", "huber", "pinball",
+                                                               "bar_distribution"], help="= --loss")
+    g.add_argument("--regression-quantiles", type=_quantile_list, default=None,
+                   help="comma-separated pinball quantiles (default: the 999-level grid)")
+    g.add_argument("--bar-borders-low", type=float, default=None, help="bar_distribution: lowest border (context std)")
+    g.add_argument("--bar-borders-high", type=float, default=None)
+    g.add_argument("--min-samples", type=int, default=None, help="= --min-rows")
+    g.add_argument("--max-samples", type=int, default=None, help="= --max-rows")
+    g.add_argument("--feature-positional-embedding-type", default=None, choices=["subortho", "learned", "none"])
+    g.add_argument("--feature-positional-embedding-num-slots", type=int, default=None)
+    g.add_argument("--column-specific-y-aware", action="store_true", help="column-specific target-aware gating")
+    g.add_argument("--no-target-aware-embedding", action="store_true")
+    g.add_argument("--no-qassmax", action="store_true", help="plain softmax in the sequence attention")
+    g.add_argument("--model-v2-lite", action="store_true", help="SwiGLU + RMSNorm + pre-norm / DeepNorm (the presets)")
+    g.add_argument("--checkpoint", default=None, help="model_config from a checkpoint (.pt / .ckpt) or JSON file")
+    g.add_argument("--resume-model-only", action="store_true", help="with --resume: weights only (= --init-from)")
+    g.add_argument("--gradient-checkpointing", action="store_true", help="layer checkpointing (the default here)")
+    g.add_argument("--task-type", default="reg", choices=["both", "cls", "reg"], help="this build trains 'reg'")
+    g.add_argument("--regression-only", action="store_true", help="regression episodes only (always, here)")
+    g.add_argument("--no-prefetch", action="store_true", help="= --prefetch-workers 0")
+    g.add_argument("--prefetch-count", type=int, default=None, help="host prefetch workers (= --prefetch-workers)")
+    g.add_argument("--context-missingness-prob", type=float, default=None,
+                   help="> 0: missing-cell augmentation with this probability (turns --augment on)")
+    g.add_argument("--heavy-tail-prior-prob", type=float, default=None,
+                   help="> 0: heavy-tailed column augmentation with this probability (turns --augment on)")
+    g.add_argument("--device", default=None, help="single-process runs: the CUDA device (default cuda:LOCAL_RANK)")
+    g.add_argument("--no-wandb", action="store_true")
+    g.add_argument("--wandb-entity", default=None)
+    g.add_argument("--wandb-group", default=None)
+    g.add_argument("--wandb-job-type", default=None)
+    g.add_argument("--wandb-tags", default=None, help="comma-separated")
+    for flag in ("--compile", "--compile-pinball-loss", "--compile-encoder-layers", "--compile-disable-ddp-optimizer",
+                 "--native-rms-norm", "--ema-foreach", "--no-mixed-precision"):
+        g.add_argument(flag, action="store_true", help="accepted; replaced here by the native kernels")
+    g.add_argument("--compile-mode", default=None, help="accepted; replaced here by the native kernels")
+    g.add_argument("--compile-cache-limit", type=int, default=None, help="accepted; replaced here by the native kernels")
+
+
+def _apply_reference_flags(args) -> list[str]:
+    """Fold the reference-named flags into this CLI's settings; returns notices to print."""
+    notes = []
+    if args.task_type != "reg":
+        raise SystemExit(f"--task-type {args.task_type}: this build trains regression only (use --task-type reg)")
+    if args.regression_loss is not None:
+        args.loss = args.regression_loss
+    if args.min_samples is not None:
+        args.min_rows = args.min_samples
+    if args.max_samples is not None:
+        args.max_rows = args.max_samples
+    if args.no_prefetch:
+        args.prefetch_workers = 0
+    elif args.prefetch_count is not None:
+        args.prefetch_workers = args.prefetch_count
+    if args.resume_model_only:
+        if not args.resume:
+            raise SystemExit("--resume-model-only needs --resume")
+        args.init_from, args.resume = args.resume, None
+    probs = {k: v for k, v in (("missing_prob", args.context_missingness_prob),
+                               ("heavy_prob", args.heavy_tail_prior_prob)) if v is not None}
+    if any(v > 0.0 for v in probs.values()):
+        if args.prior != "mixture":
+            notes.append("missing-cell / heavy-tail augmentation applies to the mixture prior (--prior mixture)")
+        args.augment = probs  # augment_table probabilities (the others keep their defaults)
+    if args.no_wandb:
+        args.wandb_project = None
+    replaced = [f for f in ("compile", "compile_pinball_loss", "compile_encoder_layers", "compile_disable_ddp_optimizer",
+                            "native_rms_norm", "ema_foreach") if getattr(args, f)]
+    if replaced or args.compile_mode or args.compile_cache_limit:
+        notes.append("compile / native-RMSNorm / foreach-EMA flags do not apply: the encoder, loss and optimizer "
+                     "already run as fused sm_100a kernels")
+    if args.no_mixed_precision:
+        notes.append("--no-mixed-precision does not apply: the native path computes in bf16 with fp32 accumulation "
+                     "and fp32 master weights")
+    return notes
 
 
 def _family_probs(args) -> dict:
@@ -196,7 +288,35 @@ def wcd_lr(step: int, base: float, warmup: int, decay_start: int, total: int, mi
 def _model_config(args) -> dict:
     from synthefy_nori_b200.models.config import apply_v2_lite, finalize_arch_config, preset_config, set_dims
 
-    cfg = preset_config(args.model)
+    if getattr(args, "checkpoint", None):
+        if args.checkpoint.endswith(".json"):
+            with open(args.checkpoint) as f:
+                cfg = json.load(f)
+        else:
+            cfg = dict(torch.load(args.checkpoint, map_location="cpu", weights_only=False)["model_config"])
+    else:
+        cfg = preset_config(args.model)
+    if getattr(args, "model_v2_lite", False):
+        apply_v2_lite(cfg)
+    if getattr(args, "feature_positional_embedding_type", None) is not None:
+        cfg["feature_positional_embedding_type"] = args.feature_positional_embedding_type
+    if getattr(args, "feature_positional_embedding_num_slots", None) is not None:
+        cfg["feature_positional_embedding_num_slots"] = args.feature_positional_embedding_num_slots
+    if getattr(args, "column_specific_y_aware", False):
+        cfg["use_column_specific_y_aware"] = True
+    if getattr(args, "no_target_aware_embedding", False):
+        cfg["use_target_aware_embedding"] = False
+    if getattr(args, "no_qassmax", False):
+        cfg["use_qassmax"] = False
+        cfg.pop("qass_mode", None)
+    dec = cfg.setdefault("decoder_config", {})
+    for src, key in (("bar_borders_low", "bar_borders_low"), ("bar_borders_high", "bar_borders_high")):
+        if getattr(args, src, None) is not None:
+            dec[key] = float(getattr(args, src))
+    if getattr(args, "regression_quantiles", None) is not None and getattr(args, "loss", "pinball") == "pinball":
+        from synthefy_nori_b200.models.config import set_regression_head
+
+        set_regression_head(cfg, quantiles=args.regression_quantiles)
     if any(v is not None for v in (args.embed_dim, args.hid_dim, args.nhead, args.nlayers)):
         set_dims(cfg, embed_dim=args.embed_dim, hid_dim=args.hid_dim, nhead=args.nhead, nlayers=args.nlayers)
         apply_v2_lite(cfg)
@@ -409,7 +529,7 @@ def main(argv=None) -> int:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    device = torch.device("cuda", local)
+    device = torch.device(args.device) if (args.device and world == 1) else torch.device("cuda", local)
     torch.cuda.set_device(device)
     if world > 1 and not dist.is_initialized():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
@@ -428,8 +548,16 @@ def main(argv=None) -> int:
     stop = args.total_steps if args.run_steps is None else min(args.total_steps, run.step + args.run_steps)
     from synthefy_nori_b200.training.metrics import MetricsSink, PhaseTimer
 
+    wandb_extra = {k: v for k, v in (("entity", args.wandb_entity), ("group", args.wandb_group),
+                                       ("job_type", args.wandb_job_type),
+                                       ("tags", args.wandb_tags.split(",") if args.wandb_tags else None))
+                   if v is not None}
     sink = MetricsSink(args.metrics_file, rank, args.wandb_project, args.wandb_name,
-                       config={k: v for k, v in vars(args).items() if isinstance(v, (int, float, str, bool))})
+                       config={k: v for k, v in vars(args).items() if isinstance(v, (int, float, str, bool))},
+                       wandb_kwargs=wandb_extra)
+    if rank == 0:
+        for note in args.notices:
+            print(f"note: {note}", flush=True)
     t0, last = time.time(), None
     try:
         while run.step < stop:

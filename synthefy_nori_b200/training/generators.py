@@ -427,9 +427,10 @@ def generate_batch(batch_size: int, n_rows: int, eval_pos: int, seed: int, devic
         xf, yf = FAMILIES[f](n_rows, n_feat[i], eval_pos, rng, gen, device)
         X[i, :, : xf.shape[1]] = xf
         y[i] = yf
-    if augment:
+    if augment:  # True, or a dict of augment_table probabilities
+        kw = augment if isinstance(augment, dict) else {}
         for i in range(batch_size):
-            augment_table(X[i], n_feat[i], eval_pos, rng, gen)
+            augment_table(X[i], n_feat[i], eval_pos, rng, gen, **kw)
     y = torch.nan_to_num(y)
     mu = y[:, :eval_pos].mean(1, keepdim=True)
     sd = y[:, :eval_pos].std(1, unbiased=False, keepdim=True)

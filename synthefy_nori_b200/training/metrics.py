@@ -78,7 +78,8 @@ class PhaseTimer:
 
 class MetricsSink:
     def __init__(self, path: str | None = None, rank: int = 0, wandb_project: str | None = None,
-                 run_name: str | None = None, config: dict | None = None, echo: bool = True):
+                 run_name: str | None = None, config: dict | None = None, echo: bool = True,
+                 wandb_kwargs: dict | None = None):
         self.rank, self.echo = rank, echo
         self.f = None
         if path and rank == 0:
@@ -89,7 +90,8 @@ class MetricsSink:
             try:
                 import wandb  # noqa: PLC0415
 
-                self.wandb = wandb.init(project=wandb_project, name=run_name, config=config or {})
+                self.wandb = wandb.init(project=wandb_project, name=run_name, config=config or {},
+                                        **(wandb_kwargs or {}))
             except Exception:  # noqa: BLE001 - optional dependency / offline machine
                 self.wandb = None
 
