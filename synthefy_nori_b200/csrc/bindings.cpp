@@ -7,6 +7,8 @@ torch::Tensor gemm_bf16(const torch::Tensor& A, const torch::Tensor& W, const c1
                         double alpha, const c10::optional<torch::Tensor>& out_opt, int64_t act);
 torch::Tensor gemm_swiglu(const torch::Tensor& A, const torch::Tensor& W, const c10::optional<torch::Tensor>& row_scale,
                           const torch::Tensor& status, int64_t bn);
+torch::Tensor gemm_swiglu_bwd(const torch::Tensor& A, const torch::Tensor& W, const c10::optional<torch::Tensor>& row_scale,
+                              const torch::Tensor& dh, const torch::Tensor& status, int64_t bn);
 torch::Tensor gemm_residual(const torch::Tensor& A, const torch::Tensor& W, const torch::Tensor& resid, double alpha,
                             const c10::optional<torch::Tensor>& sumsq, const torch::Tensor& status, int64_t bn,
                             const c10::optional<torch::Tensor>& out_opt, bool w_kn);
@@ -155,6 +157,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16", &nori::gemm_bf16);
   m.def("gemm_swiglu", &nori::gemm_swiglu);
   m.def("gemm_residual", &nori::gemm_residual);
+  m.def("gemm_swiglu_bwd", &nori::gemm_swiglu_bwd);
   m.def("gemm_wgrad", &nori::gemm_wgrad);
   m.def("attn_fwd", &nori::attn_fwd);
   m.def("attn_bwd", &nori::attn_bwd);

@@ -13,6 +13,7 @@ __all__ = [
     "gemm",
     "gemm_swiglu",
     "gemm_residual",
+    "gemm_swiglu_bwd",
     "gemm_wgrad",
     "attention_fwd",
     "attention_bwd",
@@ -83,6 +84,13 @@ def gemm(a: torch.Tensor, w: torch.Tensor, row_scale=None, bias=None, bn: int = 
 def gemm_swiglu(a: torch.Tensor, w_interleaved: torch.Tensor, row_scale=None, bn: int = 0) -> torch.Tensor:
     """``silu(a W_g^T r) * (a W_u^T r)`` with gate/up rows interleaved in one weight."""
     return _lib().gemm_swiglu(a, w_interleaved, row_scale, status_word(a.device), bn)
+
+
+def gemm_swiglu_bwd(a: torch.Tensor, w_interleaved: torch.Tensor, dh: torch.Tensor, row_scale=None,
+                    bn: int = 0) -> torch.Tensor:
+    """Interleaved (d gate, d up) of ``h = silu(g) * u`` with ``(g, u) = (a W^T) r`` recomputed
+    inside the GEMM and ``dh`` read by its epilogue (the pre-activation is never written)."""
+    return _lib().gemm_swiglu_bwd(a, w_interleaved, row_scale, dh, status_word(a.device), bn)
 
 
 def gemm_residual(a, w, resid, alpha: float, sumsq=None, bn: int = 0, out=None, w_kn: bool = False) -> torch.Tensor:

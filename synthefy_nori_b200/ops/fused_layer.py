@@ -461,9 +461,11 @@ class MlpSublayer(torch.autograd.Function):
         ops.gemm_wgrad(dout, h, dw_down, alpha=alpha)
         # recompute the pre-activation (SwiGLU: gate / up interleaved) and the activation backward
         w_gu_b = wb["w_gu"]
-        gu = ops.gemm(x, w_gu_b, row_scale=rs)  # [R, 2 hd] interleaved (SwiGLU) or [R, hd] (GELU)
-        dgu = ops.swiglu_bwd(dh, gu) if ctx.act == "swiglu" else ops.gelu_bwd(dh, gu)
-        del gu, dh
+        if ctx.act == "swiglu":  # pre-activation recomputed and differentiated inside one GEMM
+            dgu = ops.gemm_swiglu_bwd(x, w_gu_b, dh, row_scale=rs)
+        else:  # GELU: [R, hd]
+            dgu = ops.gelu_bwd(dh, ops.gemm(x, w_gu_b, row_scale=rs))
+        del dh
         xn = ops.rms_apply(x, rs)
         dw_gu = torch.zeros_like(w_gu, dtype=torch.float32)
         ops.gemm_wgrad(dgu, xn, dw_gu)

@@ -48,6 +48,10 @@ def bench_gemm(a):
         fn = lambda: ops.gemm(x, w)  # noqa: E731
     elif a.epi == "swiglu":
         fn = lambda: ops.gemm_swiglu(x, w)  # noqa: E731
+    elif a.epi == "swiglubwd":
+        dh = torch.randn(M, N // 2, device="cuda").to(torch.bfloat16)
+        rs = torch.rand(M, device="cuda") + 0.5
+        fn = lambda: ops.gemm_swiglu_bwd(x, w, dh, row_scale=rs, bn=getattr(a, "bn", 0))  # noqa: E731
     elif a.epi == "residual":
         r = torch.randn(M, N, device="cuda").to(torch.bfloat16)
         fn = lambda: ops.gemm_residual(x, w, r, 0.5)  # noqa: E731
@@ -279,6 +283,7 @@ def main():
     g.add_argument("--n", type=int, default=1344)
     g.add_argument("--k", type=int, default=448)
     g.add_argument("--epi", default="store")
+    g.add_argument("--bn", type=int, default=0, help="tile N (0: the op's default)")
     t = sub.add_parser("attn")
     t.add_argument("--bh", type=int, default=128)
     t.add_argument("--n", type=int, default=2048)

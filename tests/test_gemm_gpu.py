@@ -51,6 +51,25 @@ def test_gemm_swiglu(M, E, H):
     torch.testing.assert_close(out.float(), ref, atol=3e-2, rtol=3e-2)
 
 
+@pytest.mark.parametrize("M,E,H", [(500, 448, 1344), (129, 128, 256), (1000, 352, 704)])
+@pytest.mark.parametrize("bn", [0, 128, 256])
+def test_gemm_swiglu_bwd(M, E, H, bn):
+    """Gradient of the SwiGLU pre-activation from one GEMM (recomputed gate / up, dh read by
+    the epilogue) against autograd of the fp32 statement."""
+    torch.manual_seed(3)
+    a = _rand(M, E)
+    wg, wu = _rand(H, E, scale=E ** -0.5), _rand(H, E, scale=E ** -0.5)
+    rs = torch.rand(M, device="cuda") + 0.5
+    dh = _rand(M, H)
+    out = ops.gemm_swiglu_bwd(a, ops.interleave_swiglu_weights(wg, wu), dh, row_scale=rs, bn=bn)
+    g = (_ref(a, wg) * rs[:, None]).requires_grad_()
+    u = (_ref(a, wu) * rs[:, None]).requires_grad_()
+    (torch.nn.functional.silu(g) * u).backward(dh.float())
+    ref = torch.stack((g.grad, u.grad), 2).reshape(M, 2 * H)
+    torch.testing.assert_close(out.float(), ref, atol=3e-2, rtol=3e-2)
+    ops.check_status(a.device)
+
+
 @pytest.mark.parametrize("M,N,K", [(700, 448, 896), (64, 128, 128)])
 def test_gemm_residual(M, N, K):
     torch.manual_seed(3)
