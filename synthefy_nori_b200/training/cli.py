@@ -104,6 +104,12 @@ def parse_args(argv=None):
     g.add_argument("--icl-filter-model", default=None, help="checkpoint (or hub name) of a frozen filter model")
     g.add_argument("--icl-filter-reg-min-r2", type=float, default=0.05)
     g.add_argument("--icl-filter-max-rounds", type=int, default=6)
+    g.add_argument("--learnability-filter", action="store_true",
+                   help="keep a table only if small tree ensembles fitted on its context rows score on its queries")
+    g.add_argument("--learnability-filter-reg-min-score", type=float, default=0.10)
+    g.add_argument("--icl-scaling-filter", action="store_true",
+                   help="keep a table only if more context rows improve the tree ensembles' query score")
+    g.add_argument("--icl-scaling-min-improvement", type=float, default=0.03)
     g = ap.add_argument_group("checkpoints and logging")
     g.add_argument("--checkpoint-dir", default=None)
     g.add_argument("--save-interval", type=int, default=1000)
@@ -379,6 +385,13 @@ class Run:
 
                 path = download_checkpoint(path)
             self.icl = ICLFilter(load_model(path), device, args.icl_filter_reg_min_r2, args.icl_filter_max_rounds)
+        elif args.learnability_filter or args.icl_scaling_filter:
+            from synthefy_nori_b200.training.icl_filter import TreeLearnabilityFilter
+
+            self.icl = TreeLearnabilityFilter(args.learnability_filter_reg_min_score, args.icl_filter_max_rounds,
+                                              scaling=args.icl_scaling_filter,
+                                              min_improvement=args.icl_scaling_min_improvement,
+                                              learnability=args.learnability_filter)
         self.prefetch = None
         if args.prefetch_workers > 0:
             import functools

@@ -146,3 +146,56 @@ def test_curriculum_tier_args():
         a = parse_args(tier_args(t) + ["--checkpoint-dir", "/tmp/x"])
         assert a.max_budget == TIERS[t]["budget"] and a.gradient_accumulation == TIERS[t]["accum"]
         assert a.prior == "mixture" and a.optimizer == "muon"
+
+
+def test_tree_learnability_and_scaling_filters(monkeypatch):
+    """Learnable tables pass the tree-ensemble gate, pure-noise tables are rejected and
+    regenerated until every slot passes; the context-scaling gate keeps a table only when the
+    score at the full context beats the smallest prefix by the required margin."""
+    import torch
+
+    from synthefy_nori_b200.training.icl_filter import TreeLearnabilityFilter
+
+    g = torch.Generator().manual_seed(0)
+
+    def tables(B, learnable):
+        X = torch.randn(B, 400, 6, generator=g)
+        X[:, :, 5] = 0.0  # a padded column
+        y = (X[:, :, 0] * 2 + torch.sin(3 * X[:, :, 1])) if learnable else torch.randn(B, 400, generator=g)
+        return X, y + 0.05 * torch.randn(B, 400, generator=g)
+
+    f = TreeLearnabilityFilter(min_score=0.10)
+    Xg, yg = tables(2, True)
+    Xn, yn = tables(2, False)
+    assert f.score(Xg, yg, 300).tolist() == [1.0, 1.0]
+    assert f.score(Xn, yn, 300).tolist() == [0.0, 0.0]
+    X = torch.cat((Xg[:1], Xn[:1]))
+    y = torch.cat((yg[:1], yn[:1]))
+    calls = []
+
+    def regenerate(slots, rnd):
+        calls.append((slots, rnd))
+        return tables(len(slots), True)
+
+    X2, y2 = f.filter(X, y, 300, regenerate)
+    assert calls == [([1], 1)] and bool((f.score(X2, y2, 300) == 1).all())
+    assert f.stats["first_round_rejects"] == 1
+    # constant context targets are unhealthy: rejected without fitting
+    yc = yg.clone()
+    yc[:, :300] = 1.0
+    assert f.score(Xg, yc, 300).tolist() == [0.0, 0.0]
+    # the scaling rule, with the ensemble's scores fixed per context size
+    seen = []
+
+    def fake(rising):
+        def fit_score(Xf, yf, Xt, yt, trees, depth):
+            seen.append((len(Xf), trees, depth))
+            return 0.2 + (0.001 * len(Xf) if rising else 0.0)
+        return staticmethod(fit_score)
+
+    sc = TreeLearnabilityFilter(min_score=0.10, scaling=True, learnability=False)
+    monkeypatch.setattr(TreeLearnabilityFilter, "_fit_score", fake(True))
+    assert sc.score(Xg[:1], yg[:1], 300).tolist() == [1.0]
+    assert [k for k, _, _ in seen] == [75, 119, 188, 300] and seen[0][1:] == (10, 5)
+    monkeypatch.setattr(TreeLearnabilityFilter, "_fit_score", fake(False))
+    assert sc.score(Xg[:1], yg[:1], 300).tolist() == [0.0]
