@@ -124,3 +124,83 @@ class AutoSeasonalFeature:
 
 def default_features() -> list:
     return [RunningIndexFeature(), CalendarFeature(), AutoSeasonalFeature()]
+
+
+class PeriodicSinCosineFeature:
+    """``sin`` / ``cos`` of ``2 pi t / period`` for fixed periods, with ``t`` the row position
+    in the frame (reference ``tsfeatures/basic_features.py:103-121``: columns
+    ``sin_<suffix>`` / ``cos_<suffix>``, the suffix being the period or ``<name_suffix>_<i>``)."""
+
+    def __init__(self, periods, name_suffix: str | None = None):
+        self.raw_periods = list(periods)
+        self.periods = [float(p) for p in periods]
+        self.name_suffix = name_suffix
+
+    def generate(self, df: pd.DataFrame) -> pd.DataFrame:
+        if not self.periods:
+            return df.copy()
+        t = np.arange(len(df), dtype=np.float64)
+        cols = {}
+        for period, raw in zip(self.periods, self._labels()):
+            ang = 2.0 * np.pi * t / period
+            cols[f"sin_{raw}"], cols[f"cos_{raw}"] = np.sin(ang), np.cos(ang)
+        return pd.concat([df, pd.DataFrame(cols, index=df.index)], axis=1)
+
+    __call__ = generate
+
+    def _labels(self):
+        if self.name_suffix:
+            return [f"{self.name_suffix}_{i}" for i in range(len(self.periods))]
+        return [_period_label(p) for p in self.raw_periods]
+
+
+def _period_label(p) -> str:
+    """The period as the caller wrote it: ``7`` for ints, ``30.5`` for fractional periods."""
+    return str(p)
+
+
+def _lowess_trend(x: np.ndarray, frac: float = 0.1) -> np.ndarray:
+    """Locally weighted linear regression of ``x`` on its index (Cleveland 1979): at every
+    point a straight line is fitted to the ``ceil(frac n)`` nearest points with tricube
+    weights ``(1 - (d / d_max)^3)^3``; one pass, no robustness iterations."""
+    n = len(x)
+    t = np.arange(n, dtype=np.float64)
+    k = max(2, min(n, int(np.ceil(frac * n))))
+    trend = np.empty(n)
+    for i in range(n):
+        lo = min(max(0, i - k // 2), n - k)
+        idx = slice(lo, lo + k)
+        d = np.abs(t[idx] - t[i])
+        dmax = max(d.max(), 1e-12) * (1.0 + 1e-12)
+        w = (1.0 - (d / dmax) ** 3) ** 3
+        tw, xw = t[idx], x[idx]
+        sw = w.sum()
+        mt, mx = (w * tw).sum() / sw, (w * xw).sum() / sw
+        var = (w * (tw - mt) ** 2).sum()
+        slope = (w * (tw - mt) * (xw - mx)).sum() / var if var > 0 else 0.0
+        trend[i] = mx + slope * (t[i] - mt)
+    return trend
+
+
+def detrend(x: np.ndarray, detrend_type: str) -> np.ndarray:
+    """Remove a trend from a series (reference ``tsfeatures/auto_features.py:275-299``):
+    ``first_diff`` (differences, first element repeated), ``linear`` (least-squares line),
+    ``constant`` (the mean) or ``loess`` (a local-linear smoother over 10% of the points)."""
+    x = np.asarray(x, dtype=np.float64)
+    if detrend_type == "first_diff":
+        return np.diff(x, prepend=x[:1])
+    if detrend_type == "linear":
+        t = np.arange(len(x), dtype=np.float64)
+        A = np.stack((t, np.ones_like(t)), 1)
+        coef, *_ = np.linalg.lstsq(A, x, rcond=None)
+        return x - A @ coef
+    if detrend_type == "constant":
+        return x - x.mean()
+    if detrend_type == "loess":
+        return x - _lowess_trend(x, 0.1)
+    raise ValueError(f"Invalid detrend method: {detrend_type}")
+
+
+def split_time_series_to_X_y(df: pd.DataFrame, target_col: str = "target"):
+    """(features, target) frames of a time-series frame."""
+    return df.drop(columns=[target_col]), df[[target_col]]

@@ -57,3 +57,33 @@ def test_forecaster_local_tiny_model():
     f = NoriTSForecaster(model="nori-tiny", weights="random", device="cpu", n_estimators=1, context_length=64)
     out = f.predict(hist, fut.drop(columns="target"))
     assert out.shape == (40, 10) and np.isfinite(out.to_numpy()).all()
+
+
+def test_periodic_features_detrend_and_split():
+    import pytest
+    import numpy as np
+    import pandas as pd
+
+    from synthefy_nori_b200.nori_ts import PeriodicSinCosineFeature, detrend, split_time_series_to_X_y
+
+    df = pd.DataFrame({"target": np.arange(14.0), "x": 1.0})
+    out = PeriodicSinCosineFeature([7, 30.5]).generate(df)
+    assert out.columns.tolist() == ["target", "x", "sin_7", "cos_7", "sin_30.5", "cos_30.5"]
+    np.testing.assert_allclose(out["sin_7"].to_numpy()[[0, 7]], [0.0, 0.0], atol=1e-12)
+    np.testing.assert_allclose(out["cos_7"].to_numpy()[7], 1.0)
+    assert PeriodicSinCosineFeature([12], name_suffix="m").generate(df).columns[-2:].tolist() == ["sin_m_0", "cos_m_0"]
+    t = np.arange(200.0)
+    x = 3.0 * t + 5.0 + np.sin(t)
+    np.testing.assert_allclose(detrend(x, "linear"), np.sin(t) - np.polyval(np.polyfit(t, np.sin(t), 1), t),
+                               atol=1e-8)
+    assert detrend(x, "first_diff")[0] == 0.0 and np.allclose(detrend(x, "first_diff")[1:], np.diff(x))
+    assert abs(detrend(x, "constant").mean()) < 1e-9
+    # a straight line is its own local-linear trend
+    assert np.abs(detrend(3.0 * t + 1.0, "loess")).max() < 1e-9
+    # loess removes a slow trend but keeps a fast oscillation
+    slow = np.sin(t / 60.0) * 10 + np.sin(t * 2.5)
+    assert np.corrcoef(detrend(slow, "loess"), np.sin(t * 2.5))[0, 1] > 0.9
+    with pytest.raises(ValueError):
+        detrend(x, "spline")
+    X, y = split_time_series_to_X_y(df)
+    assert X.columns.tolist() == ["x"] and y.columns.tolist() == ["target"]
