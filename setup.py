@@ -32,6 +32,7 @@ setup(
     name="synthefy_nori_b200",
     version="0.1.0",
     packages=[d.replace(os.sep, ".") for d, _, files in os.walk("synthefy_nori_b200") if "__init__.py" in files],
+    package_data={"synthefy_nori_b200.configs": ["*.json"], "synthefy_nori_b200.evaluation.benchmark_lists": ["*.csv"]},
     entry_points={"console_scripts": [
         "synthefy-nori-b200-train = synthefy_nori_b200.training.cli:main",
         "synthefy-nori-b200-eval = synthefy_nori_b200.evaluation.cli:main",

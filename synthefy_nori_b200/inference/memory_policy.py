@@ -87,6 +87,12 @@ def int8_footprint_gb(est_bf16_gb: float, *, head_dim: int) -> float:
     return est_bf16_gb / 2.0 * (1.0 + 4.0 / max(head_dim, 1))
 
 
+class ContextTooLargeError(RuntimeError, MemoryError):
+    """The context cannot fit without a fallback the caller's policy forbids (subsampling
+    disabled). A caller condition, not a device fault; the message names the setting to change.
+    Also a ``MemoryError``, so handlers written for the memory ladder catch it."""
+
+
 class MemoryPolicy(BaseModel):
     """How ``predict`` may spend GPU memory on the context cache."""
 
@@ -175,7 +181,8 @@ class MemoryPolicy(BaseModel):
             size = i8 if use_i8 else bf16
             if size > host:
                 if not q_ok or use_i8 or i8 > host:
-                    raise MemoryError(f"streamed cache needs {size:.1f} GiB of host RAM (budget {host:.1f} GiB)")
+                    raise ContextTooLargeError(f"streamed cache needs {size:.1f} GiB of host RAM (budget {host:.1f} GiB): "
+                                               "raise host_budget_absolute_gb / host_budget_frac or use an int8 cache")
                 use_i8, size = True, i8
             upd.update(rung="stream_int8" if use_i8 else "stream_bf16", context_row_chunk=int(chunk),
                        resident_gb=2 * per_layer * min(1.0, chunk / max(n_context_rows, 1)),
@@ -198,8 +205,9 @@ class MemoryPolicy(BaseModel):
             keep = max(1, min(keep, n_context_rows))
             upd.update(rung="subsample", resident_gb=per_row * keep, dropped_context_rows=n_context_rows - keep)
         else:
-            raise MemoryError(f"context cache needs {i8:.1f} GiB even as int8 (budget {budget:.1f} GiB) and "
-                              "subsampling is disabled")
+            raise ContextTooLargeError(f"context cache needs {i8:.1f} GiB even as int8 (budget {budget:.1f} GiB) "
+                                       "and subsampling is disabled: raise elements_budget / the device budget, or "
+                                       "allow_subsample=True")
         return self.model_copy(update=upd)
 
     def next_rung(self) -> str | None:

@@ -27,6 +27,7 @@ features.
 from __future__ import annotations
 
 import copy
+import os
 import warnings
 
 import numpy as np
@@ -713,6 +714,10 @@ def resolve_inference_config(config, model=None, n_estimators: int | None = None
             else DEFAULT_INFERENCE_CONFIG
     elif config == "none":
         base = [{}]
+    elif isinstance(config, (str, os.PathLike)):  # a JSON file, or a bundled config's name
+        from synthefy_nori_b200.configs import load_config
+
+        base = list(load_config(os.fspath(config)))
     else:
         base = list(config)
     if n_estimators is not None and n_estimators > 0:
