@@ -46,17 +46,19 @@ def _layer_blocks(layer):
     Dp = -(-D // 8) * 8
     A = H * Dp
 
-    def heads(p, k0, nk, key, dst_row0):
+    def heads(p, k0, nk, key, dst_row0, shared=False):
         """``nk`` head-major slabs of ``p`` starting at slab ``k0`` -> layout rows from
-        ``dst_row0`` at the padded pitch."""
-        if Dp == D:
+        ``dst_row0`` at the padded pitch; with ``shared`` (MQA K/V) every head's rows are
+        copied from head 0."""
+        if Dp == D and not shared:
             return [(p, k0 * H * D * E, nk * H * D, E, key, dst_row0 * E, E)]
-        return [(p, ((k0 + k) * H + h) * D * E, D, E, key, (dst_row0 + k * A + h * Dp) * E, E)
+        return [(p, ((k0 + k) * H + (0 if shared else h)) * D * E, D, E, key, (dst_row0 + k * A + h * Dp) * E, E)
                 for k in range(nk) for h in range(H)]
 
     return (
-        heads(sa_self.qkv_proj_weight, 0, 3, "w_ctx", 0)
-        + heads(sa_cross.qkv_proj_weight, 1, 2, "w_ctx", 3 * A)
+        heads(sa_self.qkv_proj_weight, 0, 1, "w_ctx", 0)
+        + heads(sa_self.qkv_proj_weight, 1, 2, "w_ctx", A, shared=layer.self_share_all_kv_heads)
+        + heads(sa_cross.qkv_proj_weight, 1, 2, "w_ctx", 3 * A, shared=layer.cross_share_all_kv_heads)
         + heads(sa_cross.qkv_proj_weight, 0, 1, "w_q", 0)
         + heads(sa_self.out_proj_weight, 0, 1, "wo_self", 0)
         + heads(sa_cross.out_proj_weight, 0, 1, "wo_cross", 0)
@@ -84,6 +86,18 @@ def layout_shapes(layer) -> dict:
             "w_down": (E, hd), "w_fqkv": (3 * A, E), "w_fo": (A, E)}
 
 
+def _uncovered(ranges, numel: int) -> list:
+    """Element ranges ``[(offset, length)]`` of a parameter that no block in ``ranges`` reads."""
+    gaps, pos = [], 0
+    for off, n in sorted(ranges):
+        if off > pos:
+            gaps.append((pos, off - pos))
+        pos = max(pos, off + n)
+    if pos < numel:
+        gaps.append((pos, numel - pos))
+    return gaps
+
+
 def segment_plan(model, offsets: dict, with_gather: bool):
     """Pure planning step (no device work): ``(segments, chunks, layouts)`` where each
     segment is ``(src_flat_offset, rows, cols, (layer_index, key) | None, dst_offset,
@@ -104,7 +118,7 @@ def segment_plan(model, offsets: dict, with_gather: bool):
             if cols % 4 or drs % 4 or doff % 4 or off % 4:
                 raise ValueError("layout blocks must be 4-element aligned")
             segs.append((offsets[id(p)] + off, rows, cols, (li, key), doff, drs))
-            covered[id(p)] = covered.get(id(p), 0) + rows * cols
+            covered.setdefault(id(p), set()).add((off, rows * cols))
     from synthefy_nori_b200.ops.head import head_blocks, head_supported
 
     if head_supported(model) and all(id(p) in offsets for p in model.reg_y_decoder.parameters()):
@@ -112,18 +126,17 @@ def segment_plan(model, offsets: dict, with_gather: bool):
         layouts["head"] = shapes
         for p, off, rows, cols, key, doff, drs in blocks:
             segs.append((offsets[id(p)] + off, rows, cols, ("head", key), doff, drs))
-            covered[id(p)] = covered.get(id(p), 0) + rows * cols
+            covered.setdefault(id(p), set()).add((off, rows * cols))
     if with_gather:
         for p in model.parameters():
             if not p.requires_grad or id(p) not in offsets:
                 continue
-            got = covered.get(id(p), 0)
-            if got == p.numel():
-                continue
-            if got:
-                raise ValueError("a parameter is only partly covered by the weight layouts")
-            n4 = -(-p.numel() // 4) * 4  # flat buffers pad every parameter to 64 elements
-            segs.append((offsets[id(p)], 1, n4, None, 0, 0))
+            gaps = _uncovered(covered.get(id(p), set()), p.numel())
+            for off, n in gaps:  # elements no layout reads (a whole parameter, or MQA's unused heads)
+                if off % 4:
+                    raise ValueError("layout blocks must be 4-element aligned")
+                n4 = -(-n // 4) * 4 if off + n == p.numel() else n  # flat buffers pad each parameter
+                segs.append((offsets[id(p)] + off, 1, n4, None, 0, 0))
     chunks = []
     for si, (_, rows, cols, *_rest) in enumerate(segs):
         total = rows * cols

@@ -21,6 +21,10 @@ def _config(name):
         cfg = preset_config("nori-tiny")
         cfg["activation"] = "gelu"
         return cfg
+    if name == "mqa":  # shared K/V heads in both sequence attentions (head 0's K / V for every head)
+        cfg = preset_config("nori-tiny")
+        cfg.update(self_share_all_kv_heads=True, cross_share_all_kv_heads=True)
+        return cfg
     if name == "logn-temp":  # log-n query scaling + learnable temperature, folded into the kernels
         cfg = preset_config("nori-tiny")
         cfg.update(use_logn_attention=True, use_learnable_attn_temperature=True, attn_n_ref=64.0)
@@ -52,7 +56,7 @@ def _cos(a, b):
     return float((a @ b) / (a.norm() * b.norm() + 1e-30))
 
 
-@pytest.mark.parametrize("name", ["nori-tiny", "nori-6m", "padded", "nori-30m", "logn-temp", "gelu-mlp"])
+@pytest.mark.parametrize("name", ["nori-tiny", "nori-6m", "padded", "nori-30m", "logn-temp", "gelu-mlp", "mqa"])
 def test_native_forward_matches_fp32(name):
     m = _model(name).eval()
     x, y, ep = _data()
@@ -69,7 +73,7 @@ def test_native_forward_matches_fp32(name):
     assert _cos(auto, ref) > 0.999
 
 
-@pytest.mark.parametrize("name", ["nori-tiny", "padded", "logn-temp", "gelu-mlp"])
+@pytest.mark.parametrize("name", ["nori-tiny", "padded", "logn-temp", "gelu-mlp", "mqa"])
 def test_native_backward_matches_fp32(name):
     m = _model(name).train()
     if name == "logn-temp":  # temperatures away from 1 (and one negative: |t| is used)
@@ -109,7 +113,7 @@ def test_trainer_reduces_loss_on_fixed_batch():
     assert losses[-1] < losses[0]
 
 
-@pytest.mark.parametrize("name", ["nori-tiny", "padded", "gelu-mlp"])
+@pytest.mark.parametrize("name", ["nori-tiny", "padded", "gelu-mlp", "mqa"])
 @pytest.mark.parametrize("dtype", ["bf16", "int8"])
 def test_native_context_cache_matches_full_forward(dtype, name):
     m = _model(name).eval()

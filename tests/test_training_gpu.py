@@ -15,6 +15,8 @@ def _setup(**cfg):
 
     torch.manual_seed(0)
     mc = preset_config("nori-tiny")
+    if cfg.pop("mqa", False):  # shared K/V heads in both sequence attentions
+        mc.update(self_share_all_kv_heads=True, cross_share_all_kv_heads=True)
     if cfg.get("loss") in ("mse", "smooth_l1", "huber"):
         set_regression_head(mc, loss=cfg["loss"])
     m = build_model(mc).cuda()
@@ -24,7 +26,8 @@ def _setup(**cfg):
 
 
 @pytest.mark.parametrize("cfg", [dict(optimizer="muon", lr=2e-3), dict(loss="mse", lr=1e-3),
-                                 dict(loss="huber", lr=1e-3), dict(loss="bar_distribution", lr=1e-3)])
+                                 dict(loss="huber", lr=1e-3), dict(loss="bar_distribution", lr=1e-3),
+                                 dict(lr=1e-3, mqa=True)])
 def test_trainer_variants_reduce_loss(cfg):
     tr, b = _setup(ema_decay=0.99, **cfg)
     losses = [tr.train_step(b.x, b.y, b.eval_pos).item() for _ in range(10)]
@@ -59,3 +62,21 @@ def test_mask_prediction_training():
     losses = [tr.train_step(b.x, b.y, b.eval_pos).item() for _ in range(10)]
     assert all(torch.isfinite(torch.tensor(losses))) and losses[-1] < losses[0]
     assert m.feature_decoder[0].weight.grad is not None and m.feature_decoder[0].weight.grad.abs().sum() > 0
+
+
+def test_mqa_layouts_follow_the_optimizer():
+    """With shared K/V heads the persistent bf16 layouts written after each optimizer step
+    equal a fresh cast of the (head-0-broadcast) weights."""
+    from synthefy_nori_b200.ops.fused_layer import _bf, _pad_heads, layer_weights
+
+    tr, b = _setup(lr=1e-3, mqa=True)
+    for _ in range(2):
+        tr.train_step(b.x, b.y, b.eval_pos)
+    torch.cuda.synchronize()
+    layer = tr.model.transformer_encoder.layers[0]
+    persistent = getattr(layer, "_nori_layouts", None)
+    assert persistent is not None
+    E, H = layer.embed_dim, layer.nhead
+    D = E // H
+    want = _bf(_pad_heads(layer_weights(layer)["w_ctx"].detach(), H, D, -(-D // 8) * 8))
+    torch.testing.assert_close(persistent[1]["w_ctx"].float(), want.float(), atol=0, rtol=0)

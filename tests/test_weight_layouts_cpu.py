@@ -47,22 +47,31 @@ def _padded_head_config():
     return _preset(embed_dim=88, hid_dim=96, nhead=2, nlayers=2)
 
 
-@pytest.mark.parametrize("cfg", ["tiny", "padded"])
+def _mqa_config():
+    """nori-tiny with shared K/V heads in both sequence attentions (MQA)."""
+    cfg = preset_config("nori-tiny")
+    cfg.update(self_share_all_kv_heads=True, cross_share_all_kv_heads=True)
+    return cfg
+
+
+@pytest.mark.parametrize("cfg", ["tiny", "padded", "mqa"])
 def test_segment_plan_reproduces_cast_layouts(cfg):
     from synthefy_nori_b200.ops.fused_layer import _bf, _pad_heads, layer_weights
 
     torch.manual_seed(0)
-    model = build_model(preset_config("nori-tiny") if cfg == "tiny" else _padded_head_config())
+    model = build_model({"tiny": lambda: preset_config("nori-tiny"), "padded": _padded_head_config,
+                         "mqa": _mqa_config}[cfg]())
     params, offs, flat = _flat(model)
     segs, chunks, shapes = segment_plan(model, offs, with_gather=True)
-    # every trainable parameter is covered exactly once
+    # every trainable parameter is covered exactly once (MQA: head 0's K / V rows once per head)
     cover = torch.zeros(flat.numel(), dtype=torch.int32)
     for src, rows, cols, *_ in segs:
         assert src % 4 == 0 and cols % 4 == 0
         cover[src : src + rows * cols] += 1
     for p in params:
         o = offs[id(p)]
-        assert bool((cover[o : o + p.numel()] == 1).all())
+        c = cover[o : o + p.numel()]
+        assert bool((c == 1).all()) if cfg != "mqa" else bool((c >= 1).all())
     got = _emulate(segs, chunks, flat, shapes)
     for li, layer in enumerate(model.transformer_encoder.layers):
         w = layer_weights(layer)
