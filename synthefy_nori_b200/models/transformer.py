@@ -315,9 +315,9 @@ class FeaturesTransformer(nn.Module):
             if not getattr(self, "_nori_warned_variant", False):
                 import warnings
 
-                warnings.warn("the native sm_100a kernels do not cover this encoder-layer variant (log-n or learnable "
-                              "attention temperature, qk-norm, shared K/V heads, a non-SwiGLU MLP, the fmfmsm arch "
-                              "or post-norm); running the PyTorch path", RuntimeWarning, stacklevel=3)
+                warnings.warn("the native sm_100a kernels do not cover this encoder-layer variant (qk-norm in the "
+                              "one-phase encoder, a LayerNorm layer, a head wider than 64, the fmfmsm arch or "
+                              "post-norm); running the PyTorch path", RuntimeWarning, stacklevel=3)
                 self._nori_warned_variant = True
             return False
         return True
