@@ -199,3 +199,39 @@ def test_tree_learnability_and_scaling_filters(monkeypatch):
     assert [k for k, _, _ in seen] == [75, 119, 188, 300] and seen[0][1:] == (10, 5)
     monkeypatch.setattr(TreeLearnabilityFilter, "_fit_score", fake(False))
     assert sc.score(Xg[:1], yg[:1], 300).tolist() == [0.0]
+
+
+def test_memory_plan_arithmetic(monkeypatch):
+    """The training step's memory plan (host arithmetic, with the device queries faked): the
+    attention stash needs all layers' outputs within a quarter of the available memory, and
+    the trailing layers that skip checkpointing fit next to the checkpointed ones."""
+    import torch
+
+    from synthefy_nori_b200.models.config import preset_config
+    from synthefy_nori_b200.ops import fused_layer
+    from synthefy_nori_b200.ops.fused_layer import Geometry, _layer_bytes, memory_plan
+    from synthefy_nori_b200.utils.loading import build_model
+
+    model = build_model(preset_config("nori-100m"))
+    GiB = 2 ** 30
+
+    class Props:
+        total_memory = 180 * GiB
+
+    monkeypatch.setattr(torch.cuda, "get_device_properties", lambda d: Props())
+    dev = torch.device("cuda", 0)
+
+    def plan(avail_gib, rows):
+        monkeypatch.setattr(fused_layer, "_available_bytes", lambda d: int(avail_gib * GiB))
+        g = Geometry(B=16, ep=rows * 2 // 3, nq=rows - rows * 2 // 3, T=51, E=448, H=8)
+        return memory_plan(model, g, dev), _layer_bytes(model, g)
+
+    (stash, plain), (x_b, stash_b, full_b) = plan(170, 1200)
+    assert stash and 0 < plain < 26 and x_b < stash_b < full_b
+    (stash_big, plain_big), _ = plan(170, 2048)
+    assert plain_big < plain  # bigger tables keep fewer layers un-checkpointed
+    (stash_low, plain_low), _ = plan(20, 1200)
+    assert not stash_low and plain_low == 0  # little memory: full checkpointing, no stash
+    monkeypatch.setenv("NORI_PLAIN_LAYERS", "3")
+    assert plan(170, 1200)[0][1] == 3
+    assert memory_plan(model, Geometry(B=1, ep=8, nq=4, T=3, E=448, H=8), torch.device("cpu")) == (False, 0)
